@@ -1,0 +1,104 @@
+/* C ABI of the b200 Laya decision engine (liblaya_b200.so).
+ *
+ * Plain pointers and sizes only; every function returns 0 on success and a
+ * nonzero status on failure, never throws across the boundary, and leaves a
+ * message readable through laya_b200_last_error().  One engine owns one GPU:
+ * its weights, activation arena, CUDA-graph slots, streams and pinned I/O
+ * buffers.  Calls on one engine must be serialised by the caller (the Python
+ * B200Engine holds a lock, as BlackwellEngine does at
+ * src/laya_blackwell/engine.py:84,192).  Different engines (different GPUs)
+ * may be driven from different threads concurrently.
+ */
+#ifndef LAYA_B200_H
+#define LAYA_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define LAYA_B200_API __attribute__((visibility("default")))
+#else
+#define LAYA_B200_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct laya_b200_engine laya_b200_engine;
+
+/* Network shape.  Mirrors the checkpoint's encoder config and the Laya head
+ * that FastDecisionModel reads (src/laya_blackwell/model.py:37-56,82-83). */
+typedef struct laya_b200_config {
+  int32_t layers, hidden, heads, head_dim, intermediate, vocab, max_len;
+  int32_t local_window;   /* radius: local layers see |q-k| <= local_window (model.py:82-83) */
+  int32_t global_every;   /* layer i is global iff i % global_every == 0 */
+  float rope_theta_global, rope_theta_local, norm_eps;
+  int32_t head_layers, head_heads, head_ff, num_qtypes, act_hidden;
+  int32_t max_batch;      /* largest padded batch any captured shape may use */
+  int32_t max_options;    /* largest padded option count */
+} laya_b200_config;
+
+enum { LAYA_B200_BF16 = 0, LAYA_B200_FP8 = 1, LAYA_B200_NVFP4 = 2 };
+
+/* Replaces the model construction of BlackwellEngine.__init__
+ * (src/laya_blackwell/engine.py:74-104): select the GPU, validate the shape,
+ * allocate the weight and activation arenas. */
+LAYA_B200_API int laya_b200_create(int device, const laya_b200_config* cfg, laya_b200_engine** out);
+
+/* Upload one parameter by its table name (e.g. "enc.3.wqkv"), host bytes in
+ * the storage dtype (bf16 bit patterns for Linear weights/biases, fp32 for
+ * embeddings and LayerNorms), replacing FastDecisionModel's bf16 casts
+ * (model.py:28-35).  Sizes are checked against the table. */
+LAYA_B200_API int laya_b200_set_weight(laya_b200_engine* e, const char* name, const void* host, size_t bytes);
+
+/* Check that every parameter was uploaded, run the offline packer for the
+ * precision (LAYA_B200_FP8: per-output-row e4m3 like
+ * quantization.py:62-73; LAYA_B200_NVFP4: e2m1 + e4m3/16 + fp32 tensor
+ * scale) and build the weight tensor maps. */
+LAYA_B200_API int laya_b200_finalize(laya_b200_engine* e, int precision);
+
+/* Capture the forward for one padded shape into CUDA graphs (the analogue
+ * of BlackwellEngine._slot, engine.py:161-187).  `unmasked` mirrors the
+ * graph key's flag (engine.py:132-138); results do not depend on it. */
+LAYA_B200_API int laya_b200_capture(laya_b200_engine* e, int batch, int seq, int options, int unmasked, int* slot);
+
+/* Drop a captured slot (LRU eviction, engine.py:167-169). */
+LAYA_B200_API int laya_b200_release(laya_b200_engine* e, int slot);
+
+/* One forward on host buffers: pack into pinned memory, replay the graph
+ * (H2D copy, kernels, D2H copy), synchronise, write the outputs.  Inputs are
+ * the padded arrays of BlackwellEngine._fill (engine.py:140-153):
+ * input_ids/attention_mask [batch][seq] int64, marker_pos [batch][options]
+ * int64, marker_mask [batch][options] uint8, qtype [batch] int64.  Outputs:
+ * logits [batch][options] fp32 (masked options = -1e4), act [batch][2] fp32
+ * (model.py:115,122).  Replaces engine.py:205-212 and host.cpp:64-73. */
+LAYA_B200_API int laya_b200_run(laya_b200_engine* e, int slot, const int64_t* input_ids, const int64_t* attention_mask,
+                  const int64_t* marker_pos, const uint8_t* marker_mask, const int64_t* qtype, float* logits,
+                  float* act);
+
+/* Benchmark helper: replay the kernels-only graph `iterations` times on the
+ * inputs already resident on the device (from the last run) and return the
+ * mean device time per forward in milliseconds (CUDA events). */
+LAYA_B200_API int laya_b200_replay_device(laya_b200_engine* e, int slot, int iterations, float* ms_per_forward);
+
+/* Number of kernels one forward of the slot launches. */
+LAYA_B200_API int laya_b200_kernel_count(laya_b200_engine* e, int slot, int* count);
+
+/* Test hook with no counterpart in the reference: copy the first `bytes` of
+ * a named activation buffer ("h", "n", "qkv", "attn", "g", "hsel", "msc",
+ * "zsc") to host memory after synchronising, so kernel-level tests can
+ * compare intermediate results with a CPU oracle. */
+LAYA_B200_API int laya_b200_read_buffer(laya_b200_engine* e, const char* name, void* dst, size_t bytes);
+
+/* Last error message of the engine (or of the last failed create when e is
+ * NULL).  The pointer stays valid until the next call on the engine. */
+LAYA_B200_API const char* laya_b200_last_error(laya_b200_engine* e);
+
+/* Synchronise, free every device resource.  Safe on NULL. */
+LAYA_B200_API int laya_b200_destroy(laya_b200_engine* e);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

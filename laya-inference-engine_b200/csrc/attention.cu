@@ -1,0 +1,238 @@
+// Fused RoPE attention for the encoder (global and radius-64 local layers)
+// and the head's key-padded attention.  Replaces rope_qkv + SDPA
+// (src/laya_blackwell/model.py:92-96 and :62-67, kernels.py:62-93).
+//
+// One CTA = 64 queries of one (sequence, head); 4 warps x 16 queries.
+// Q and K are rotated while they are staged to shared memory, with the
+// reference's rounding: y = bf16(fl(a*cos) + fl(b*sin)) in fp32 without FMA
+// contraction.  Local layers only visit key tiles inside [q-64, q+64]
+// (compute skipping, not just masking).  Scores and the online softmax are
+// fp32; P is rounded to bf16 for the P.V product (as FlashAttention does);
+// a query that sees no key returns zeros (SDPA's result for a fully masked row).
+#include "common.cuh"
+#include "params.h"
+#include "launch.h"
+
+namespace laya {
+
+namespace {
+constexpr int AQ = 64;    // queries per CTA
+constexpr int AK = 64;    // keys per tile
+constexpr int LDS = 72;   // padded shared row (bf16 elements)
+
+DEVI void ldsm_x4(uint32_t (&r)[4], const void* p) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(smem_u32(p)));
+}
+DEVI void ldsm_x4_t(uint32_t (&r)[4], const void* p) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(smem_u32(p)));
+}
+DEVI void mma16816(float (&c)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};"
+      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+DEVI uint32_t pack_bf16(float lo, float hi) {
+  __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&v);
+}
+
+// Rotate 8 dims [c, c+8) (c < 32) together with their partners [c+32, c+40).
+DEVI void rope8(uint4& lo, uint4& hi, const float* cs, const float* sn, int c) {
+  __nv_bfloat16* xl = reinterpret_cast<__nv_bfloat16*>(&lo);
+  __nv_bfloat16* xh = reinterpret_cast<__nv_bfloat16*>(&hi);
+#pragma unroll
+  for (int e = 0; e < 8; ++e) {
+    const float a = __bfloat162float(xl[e]);
+    const float b = __bfloat162float(xh[e]);
+    const float yl = __fadd_rn(__fmul_rn(a, cs[c + e]), __fmul_rn(-b, sn[c + e]));
+    const float yh = __fadd_rn(__fmul_rn(b, cs[c + e + 32]), __fmul_rn(a, sn[c + e + 32]));
+    xl[e] = __float2bfloat16_rn(yl);
+    xh[e] = __float2bfloat16_rn(yh);
+  }
+}
+}  // namespace
+
+__global__ void __launch_bounds__(128) attention_kernel(const AttnParams p) {
+  __shared__ __align__(16) __nv_bfloat16 sQ[AQ * LDS];
+  __shared__ __align__(16) __nv_bfloat16 sK[AK * LDS];
+  __shared__ __align__(16) __nv_bfloat16 sV[AK * LDS];
+  __shared__ int s_qpos[AQ];
+  __shared__ int s_kvalid[AK];
+
+  griddep_launch_dependents();
+  const int q0 = blockIdx.x * AQ, h = blockIdx.y, b = blockIdx.z;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  griddep_wait();
+
+  if (tid < AQ) {
+    const int qi = q0 + tid;
+    s_qpos[tid] = qi < p.nq ? (p.q_pos ? p.q_pos[b * p.nq + qi] : qi) : -1;
+  }
+  __syncthreads();
+  const size_t seq_base = (size_t)b * p.s;
+  for (int it = tid; it < AQ * 4; it += 128) {
+    const int r = it >> 2, c = (it & 3) * 8;
+    const int pos = s_qpos[r];
+    uint4 lo = make_uint4(0, 0, 0, 0), hi = lo;
+    if (pos >= 0) {
+      const __nv_bfloat16* src = p.qkv + (seq_base + pos) * p.ld_qkv + h * 64;
+      lo = *reinterpret_cast<const uint4*>(src + c);
+      hi = *reinterpret_cast<const uint4*>(src + c + 32);
+      if (p.cos) rope8(lo, hi, p.cos + (size_t)pos * 64, p.sin + (size_t)pos * 64, c);
+    }
+    *reinterpret_cast<uint4*>(&sQ[r * LDS + c]) = lo;
+    *reinterpret_cast<uint4*>(&sQ[r * LDS + c + 32]) = hi;
+  }
+
+  int kbeg = 0, kend = p.s;
+  if (p.window >= 0) {  // queries of this tile are positions q0 .. q0+63
+    const int qmax = min(q0 + AQ, p.nq) - 1;
+    kbeg = max(0, q0 - p.window);
+    kend = min(p.s, qmax + p.window + 1);
+    kbeg = (kbeg / AK) * AK;
+  }
+  __syncthreads();
+
+  uint32_t qf[4][4];
+#pragma unroll
+  for (int ks = 0; ks < 4; ++ks)
+    ldsm_x4(qf[ks], &sQ[(warp * 16 + (lane & 7) + ((lane >> 3) & 1) * 8) * LDS + ks * 16 + (lane >> 4) * 8]);
+
+  const int g = lane >> 2, t4 = lane & 3;
+  const int qpos0 = s_qpos[warp * 16 + g], qpos1 = s_qpos[warp * 16 + g + 8];
+  const float kScaleLog2 = 0.125f * 1.4426950408889634f;
+  float o[8][4];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
+  float mrow[2] = {-INFINITY, -INFINITY}, lrow[2] = {0.f, 0.f};
+
+  for (int k0 = kbeg; k0 < kend; k0 += AK) {
+    __syncthreads();
+    for (int it = tid; it < AK * 4; it += 128) {
+      const int r = it >> 2, c = (it & 3) * 8;
+      const int kp = k0 + r;
+      uint4 klo = make_uint4(0, 0, 0, 0), khi = klo, vlo = klo, vhi = klo;
+      if (kp < p.s) {
+        const __nv_bfloat16* row = p.qkv + (seq_base + kp) * p.ld_qkv;
+        const __nv_bfloat16* ks = row + p.d + h * 64;
+        const __nv_bfloat16* vs = row + 2 * p.d + h * 64;
+        klo = *reinterpret_cast<const uint4*>(ks + c);
+        khi = *reinterpret_cast<const uint4*>(ks + c + 32);
+        vlo = *reinterpret_cast<const uint4*>(vs + c);
+        vhi = *reinterpret_cast<const uint4*>(vs + c + 32);
+        if (p.cos) rope8(klo, khi, p.cos + (size_t)kp * 64, p.sin + (size_t)kp * 64, c);
+      }
+      *reinterpret_cast<uint4*>(&sK[r * LDS + c]) = klo;
+      *reinterpret_cast<uint4*>(&sK[r * LDS + c + 32]) = khi;
+      *reinterpret_cast<uint4*>(&sV[r * LDS + c]) = vlo;
+      *reinterpret_cast<uint4*>(&sV[r * LDS + c + 32]) = vhi;
+    }
+    if (tid < AK) s_kvalid[tid] = (k0 + tid < p.s) ? (p.key_valid[seq_base + k0 + tid] != 0) : 0;
+    __syncthreads();
+
+    float sc[8][4];
+#pragma unroll
+    for (int nt = 0; nt < 8; ++nt) {
+      sc[nt][0] = sc[nt][1] = sc[nt][2] = sc[nt][3] = 0.f;
+#pragma unroll
+      for (int kk = 0; kk < 2; ++kk) {
+        uint32_t kb[4];
+        ldsm_x4(kb, &sK[(nt * 8 + (lane & 7)) * LDS + kk * 32 + (lane >> 3) * 8]);
+        mma16816(sc[nt], qf[2 * kk], kb[0], kb[1]);
+        mma16816(sc[nt], qf[2 * kk + 1], kb[2], kb[3]);
+      }
+    }
+    // mask, scale to log2 domain, tile row max
+    float tmax[2] = {-INFINITY, -INFINITY};
+#pragma unroll
+    for (int nt = 0; nt < 8; ++nt) {
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int kl = nt * 8 + 2 * t4 + (e & 1);
+        const int kp = k0 + kl;
+        const int qp = (e >> 1) ? qpos1 : qpos0;
+        bool vis = s_kvalid[kl] && qp >= 0;
+        if (p.window >= 0) vis = vis && abs(qp - kp) <= p.window;
+        const float v = vis ? sc[nt][e] * kScaleLog2 : -INFINITY;
+        sc[nt][e] = v;
+        tmax[e >> 1] = fmaxf(tmax[e >> 1], v);
+      }
+    }
+#pragma unroll
+    for (int r = 0; r < 2; ++r) {
+      tmax[r] = fmaxf(tmax[r], __shfl_xor_sync(0xffffffffu, tmax[r], 1));
+      tmax[r] = fmaxf(tmax[r], __shfl_xor_sync(0xffffffffu, tmax[r], 2));
+      const float mnew = fmaxf(mrow[r], tmax[r]);
+      const float msafe = mnew == -INFINITY ? 0.f : mnew;
+      const float corr = exp2f(mrow[r] - msafe);
+      lrow[r] *= corr;
+#pragma unroll
+      for (int nt = 0; nt < 8; ++nt) {
+        o[nt][2 * r] *= corr;
+        o[nt][2 * r + 1] *= corr;
+      }
+      mrow[r] = mnew;
+#pragma unroll
+      for (int nt = 0; nt < 8; ++nt) {
+        const float p0 = exp2f(sc[nt][2 * r] - msafe);
+        const float p1 = exp2f(sc[nt][2 * r + 1] - msafe);
+        sc[nt][2 * r] = p0;
+        sc[nt][2 * r + 1] = p1;
+        lrow[r] += p0 + p1;
+      }
+    }
+    // O += P V
+#pragma unroll
+    for (int ks = 0; ks < 4; ++ks) {
+      uint32_t pa[4];
+      pa[0] = pack_bf16(sc[2 * ks][0], sc[2 * ks][1]);
+      pa[1] = pack_bf16(sc[2 * ks][2], sc[2 * ks][3]);
+      pa[2] = pack_bf16(sc[2 * ks + 1][0], sc[2 * ks + 1][1]);
+      pa[3] = pack_bf16(sc[2 * ks + 1][2], sc[2 * ks + 1][3]);
+#pragma unroll
+      for (int nt2 = 0; nt2 < 4; ++nt2) {
+        uint32_t vb[4];
+        ldsm_x4_t(vb, &sV[(ks * 16 + (lane & 7) + ((lane >> 3) & 1) * 8) * LDS + nt2 * 16 + (lane >> 4) * 8]);
+        mma16816(o[2 * nt2], pa, vb[0], vb[1]);
+        mma16816(o[2 * nt2 + 1], pa, vb[2], vb[3]);
+      }
+    }
+  }
+
+#pragma unroll
+  for (int r = 0; r < 2; ++r) {
+    float l = lrow[r];
+    l += __shfl_xor_sync(0xffffffffu, l, 1);
+    l += __shfl_xor_sync(0xffffffffu, l, 2);
+    const float inv = l > 0.f ? 1.f / l : 0.f;
+    const int qi = q0 + warp * 16 + g + 8 * r;
+    if (qi < p.nq) {
+      __nv_bfloat16* dst = p.out + ((size_t)b * p.nq + qi) * p.ld_out + h * 64;
+#pragma unroll
+      for (int nt = 0; nt < 8; ++nt)
+        *reinterpret_cast<uint32_t*>(dst + nt * 8 + 2 * t4) = pack_bf16(o[nt][2 * r] * inv, o[nt][2 * r + 1] * inv);
+    }
+  }
+}
+
+cudaError_t launch_attention(const AttnParams& p, int batch, int heads, cudaStream_t stream, bool pdl) {
+  if (p.window >= 0 && p.q_pos) return cudaErrorInvalidValue;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((p.nq + AQ - 1) / AQ, heads, batch);
+  cfg.blockDim = dim3(128, 1, 1);
+  cfg.stream = stream;
+  cudaLaunchAttribute attr;
+  attr.id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr.val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = &attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, attention_kernel, p);
+}
+
+}  // namespace laya

@@ -1,0 +1,931 @@
+// Host runtime behind the C ABI (include/laya_b200.h): weight arena and
+// packing, activation arena, per-shape CUDA-graph slots with pinned I/O, and
+// the forward's launch sequence.
+//
+// The forward mirrors FastDecisionModel.forward
+// (src/laya_blackwell/model.py:72-123); the slot / fill / replay logic mirrors
+// BlackwellEngine._slot / _fill / run_prepared (src/laya_blackwell/engine.py:
+// 140-214) and the fast mode's in-graph copies (src/laya_blackwell/fast/
+// host.py:192-199, fast/native/host.cpp:15-80).
+#include "laya_b200.h"
+#include "common.cuh"
+#include "launch.h"
+#include "params.h"
+
+#include <cmath>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <functional>
+#include <map>
+#include <memory>
+#include <mutex>
+#include <string>
+#include <vector>
+
+using namespace laya;
+
+namespace {
+
+thread_local std::string g_create_error;
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn get_encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  });
+  return fn;
+}
+
+struct Error {
+  std::string msg;
+};
+
+[[noreturn]] void fail(const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  throw Error{buf};
+}
+
+void ck(cudaError_t e, const char* what) {
+  if (e != cudaSuccess) fail("%s: %s", what, cudaGetErrorString(e));
+}
+
+enum Dtype { kBf16 = 0, kF32 = 1 };
+
+struct ParamInfo {
+  size_t elems;
+  int dtype;
+  size_t offset;  // bytes into the weight arena
+  int rows, cols;
+  bool uploaded;
+};
+
+size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
+
+// K-major 2D tensor map with 128-byte swizzle: rows x cols elements of
+// `esize` bytes (cols*esize a multiple of 16), box = (128 bytes) x box_rows.
+CUtensorMap make_map(const void* ptr, int rows, int cols, int esize, int box_rows) {
+  EncodeTiledFn enc = get_encode_fn();
+  if (!enc) fail("cuTensorMapEncodeTiled is unavailable");
+  CUtensorMap m;
+  const CUtensorMapDataType dt = esize == 2 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_UINT8;
+  cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)cols * esize};
+  cuuint32_t box[2] = {(cuuint32_t)(128 / esize), (cuuint32_t)box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = enc(&m, dt, 2, const_cast<void*>(ptr), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                   CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) fail("cuTensorMapEncodeTiled failed (%d) rows=%d cols=%d", (int)r, rows, cols);
+  return m;
+}
+
+// One projection weight as the GEMM consumes it.
+struct Proj {
+  int N = 0, K = 0, kind = kKindBf16;
+  const void* w = nullptr;           // bf16 [N][K] or e4m3 [N][K]
+  const float* w_scale = nullptr;    // fp8 per-row scales
+  const __nv_bfloat16* bias = nullptr;
+  CUtensorMap map;
+};
+
+struct Shape {
+  int b, s, k, unmasked;
+};
+
+struct Slot {
+  Shape sh;
+  cudaGraphExec_t io_exec = nullptr;   // H2D + kernels + D2H
+  cudaGraphExec_t dev_exec = nullptr;  // kernels only
+  int kernels = 0;
+  bool live = false;
+};
+
+}  // namespace
+
+struct laya_b200_engine {
+  int device = 0;
+  laya_b200_config cfg{};
+  int precision = -1;
+  int sm_count = 148;
+  bool finalized = false;
+  std::string last_error;
+  cudaStream_t stream = nullptr;
+  cudaEvent_t ev0 = nullptr, ev1 = nullptr;
+
+  std::map<std::string, ParamInfo> params;
+  uint8_t* warena = nullptr;
+  size_t warena_bytes = 0;
+  uint8_t* qarena = nullptr;  // packed low-precision encoder weights
+  size_t qarena_bytes = 0;
+
+  // activations
+  uint8_t* aarena = nullptr;
+  size_t aarena_bytes = 0;
+  int max_tokens = 0, max_rows_sel = 0, max_rows_score = 0;
+  float* h = nullptr;
+  __nv_bfloat16 *n = nullptr, *qkv = nullptr, *attn = nullptr, *g = nullptr;
+  uint8_t *n8 = nullptr, *a8 = nullptr, *g8 = nullptr;
+  float *n8s = nullptr, *a8s = nullptr, *g8s = nullptr;
+  float* hsel = nullptr;
+  __nv_bfloat16 *asel = nullptr, *nsel = nullptr, *fsel = nullptr, *msc = nullptr, *zsc = nullptr;
+  float *gcos = nullptr, *gsin = nullptr, *lcos = nullptr, *lsin = nullptr;
+  // device inputs / outputs (int32 staging layout)
+  int32_t* d_in = nullptr;
+  float* d_out = nullptr;
+  int32_t* h_in = nullptr;  // pinned
+  float* h_out = nullptr;   // pinned
+  size_t in_words = 0, out_words = 0;
+  uint32_t* status_host = nullptr;  // mapped pinned
+  uint32_t* status_dev = nullptr;
+
+  // projections
+  std::vector<Proj> wqkv, wo, wi, wo2;
+  std::vector<Proj> in_proj, out_proj, lin1, lin2;
+  Proj sc_fc1;
+
+  std::vector<Slot> slots;
+  int launches = 0;  // counter while enqueuing
+
+  // input section offsets (words), computed from the capacity
+  size_t off_ids = 0, off_valid = 0, off_qtype = 0, off_mmask = 0, off_selsrc = 0, off_selpos = 0,
+         off_score = 0;
+};
+
+namespace {
+
+// -------------------------------------------------------------- param table
+// Same order and shapes as laya_b200.weights.param_table.
+std::vector<std::tuple<std::string, int, int, int>> param_table(const laya_b200_config& c) {
+  std::vector<std::tuple<std::string, int, int, int>> t;  // name, rows, cols, dtype
+  const int d = c.hidden, I = c.intermediate, V = c.vocab, F = c.head_ff, A = c.act_hidden;
+  t.emplace_back("embed.tok", V, d, kF32);
+  t.emplace_back("embed.norm.w", 1, d, kF32);
+  for (int i = 0; i < c.layers; ++i) {
+    const std::string p = "enc." + std::to_string(i) + ".";
+    if (i > 0) t.emplace_back(p + "attn_norm.w", 1, d, kF32);
+    t.emplace_back(p + "wqkv", 3 * d, d, kBf16);
+    t.emplace_back(p + "wo", d, d, kBf16);
+    t.emplace_back(p + "mlp_norm.w", 1, d, kF32);
+    t.emplace_back(p + "wi", 2 * I, d, kBf16);
+    t.emplace_back(p + "wo2", d, I, kBf16);
+  }
+  t.emplace_back("final_norm.w", 1, d, kF32);
+  t.emplace_back("type_emb", c.num_qtypes, d, kF32);
+  for (int j = 0; j < c.head_layers; ++j) {
+    const std::string p = "head." + std::to_string(j) + ".";
+    t.emplace_back(p + "norm1.w", 1, d, kF32);
+    t.emplace_back(p + "norm1.b", 1, d, kF32);
+    t.emplace_back(p + "in_proj.w", 3 * d, d, kBf16);
+    t.emplace_back(p + "in_proj.b", 1, 3 * d, kBf16);
+    t.emplace_back(p + "out_proj.w", d, d, kBf16);
+    t.emplace_back(p + "out_proj.b", 1, d, kBf16);
+    t.emplace_back(p + "norm2.w", 1, d, kF32);
+    t.emplace_back(p + "norm2.b", 1, d, kF32);
+    t.emplace_back(p + "linear1.w", F, d, kBf16);
+    t.emplace_back(p + "linear1.b", 1, F, kBf16);
+    t.emplace_back(p + "linear2.w", d, F, kBf16);
+    t.emplace_back(p + "linear2.b", 1, d, kBf16);
+  }
+  t.emplace_back("scorer.norm.w", 1, d, kF32);
+  t.emplace_back("scorer.norm.b", 1, d, kF32);
+  t.emplace_back("scorer.fc1.w", d, d, kBf16);
+  t.emplace_back("scorer.fc1.b", 1, d, kBf16);
+  t.emplace_back("scorer.fc2.w", 1, d, kBf16);
+  t.emplace_back("scorer.fc2.b", 1, 1, kBf16);
+  t.emplace_back("act.fc1.w", A, d + 4, kBf16);
+  t.emplace_back("act.fc1.b", 1, A, kBf16);
+  t.emplace_back("act.fc2.w", 2, A, kBf16);
+  t.emplace_back("act.fc2.b", 1, 2, kBf16);
+  return t;
+}
+
+template <class T>
+T* wptr(laya_b200_engine* e, const std::string& name) {
+  auto it = e->params.find(name);
+  if (it == e->params.end()) fail("no parameter %s", name.c_str());
+  return reinterpret_cast<T*>(e->warena + it->second.offset);
+}
+
+void validate_cfg(const laya_b200_config& c) {
+  if (c.head_dim != 64) fail("head_dim must be 64");
+  if (c.hidden != c.heads * c.head_dim) fail("hidden must equal heads*head_dim");
+  if (c.hidden % 128 || c.hidden < 128 || c.hidden > 1024) fail("hidden must be a multiple of 128 in [128, 1024]");
+  if (c.intermediate % 64 || c.intermediate <= 0) fail("intermediate must be a positive multiple of 64");
+  if (c.head_ff % 128 || c.head_ff <= 0) fail("head_ff must be a positive multiple of 128");
+  if (c.hidden / c.head_heads != 64 || c.hidden % c.head_heads) fail("head attention needs 64-wide heads");
+  if (c.layers < 1 || c.vocab < 1 || c.num_qtypes < 1 || c.head_layers < 0) fail("bad layer / vocab counts");
+  if (c.max_len < 1 || c.max_len > 8192) fail("max_len out of range");
+  if (c.global_every < 1 || c.local_window < 0) fail("bad attention pattern");
+  if (c.act_hidden < 32 || c.act_hidden > 1024 || c.act_hidden % 32) fail("act_hidden must be a multiple of 32");
+  if (c.max_batch < 1 || c.max_options < 2 || c.max_options > 256) fail("max_batch >= 1, 2 <= max_options <= 256");
+}
+
+// Rotary tables like transformers' default rope: inv_freq in fp32, the angle
+// pos*inv_freq in fp32, cos/sin of that fp32 angle.
+void rope_tables(float theta, int max_len, std::vector<float>& cs, std::vector<float>& sn) {
+  cs.assign((size_t)max_len * 64, 0.f);
+  sn.assign((size_t)max_len * 64, 0.f);
+  float inv[32];
+  for (int i = 0; i < 32; ++i) inv[i] = 1.0f / std::pow(theta, (float)(2 * i) / 64.0f);
+  for (int p = 0; p < max_len; ++p)
+    for (int i = 0; i < 64; ++i) {
+      const float ang = (float)p * inv[i & 31];
+      cs[(size_t)p * 64 + i] = (float)std::cos((double)ang);
+      sn[(size_t)p * 64 + i] = (float)std::sin((double)ang);
+    }
+}
+
+// ------------------------------------------------------------ the forward
+struct Fwd {
+  laya_b200_engine* e;
+  cudaStream_t st;
+  bool first = true;
+
+  bool pdl() {
+    const bool r = !first;
+    first = false;
+    return r;
+  }
+  void count(cudaError_t err, const char* what) {
+    ck(err, what);
+    ck(cudaGetLastError(), what);
+    e->launches++;
+  }
+
+  void gemm(const Proj& w, const void* x, const float* x_scale, int M, int epi, __nv_bfloat16* out, int ldo,
+            float* resid, int ldr) {
+    const int bn = gemm_token_tile(M);
+    const int esize = w.kind == kKindBf16 ? 2 : 1;
+    CUtensorMap xmap = make_map(x, M, w.K, esize, bn);
+    GemmParams p{};
+    p.M = M;
+    p.N = w.N;
+    p.K = w.K;
+    p.kblocks = (w.K + gemm_k_elems(w.kind) - 1) / gemm_k_elems(w.kind);
+    p.epilogue = epi;
+    p.out = out;
+    p.ldo = ldo;
+    p.resid = resid;
+    p.ldr = ldr;
+    p.bias = w.bias;
+    p.a_scale = x_scale;
+    p.w_scale = w.w_scale;
+    p.status = e->status_dev;
+    const int tiles = (w.N / 128) * ((M + bn - 1) / bn);
+    const int split = gemm_split(tiles, p.kblocks, e->sm_count, 8);
+    count(launch_gemm(w.kind, w.map, xmap, p, bn, split, st, pdl()), "gemm launch");
+  }
+
+  void norm(NormParams p) {
+    p.eps = e->cfg.norm_eps;
+    p.d = e->cfg.hidden;
+    count(launch_norm(p, st, pdl()), "norm launch");
+  }
+
+  void attention(const AttnParams& p, int batch, int heads) {
+    count(launch_attention(p, batch, heads, st, pdl()), "attention launch");
+  }
+
+  void run(const Shape& sh) {
+    laya_b200_engine& E = *e;
+    const laya_b200_config& c = E.cfg;
+    const int b = sh.b, s = sh.s, k = sh.k, d = c.hidden, I = c.intermediate, F = c.head_ff;
+    const int T = b * s, R = b * (1 + k), BK = b * k;
+    const bool fp8 = E.precision == LAYA_B200_FP8;
+    const int32_t* in = E.d_in;
+    const int* ids = in + E.off_ids;
+    const int* valid = in + E.off_valid;
+    const int* qtype = in + E.off_qtype;
+    const int* mmask = in + E.off_mmask;
+    const int* selsrc = in + E.off_selsrc;
+    const int* selpos = in + E.off_selpos;
+    const int* score_rows = in + E.off_score;
+
+    // enc.embeddings: gather + LayerNorm; layer 0 consumes bf16(h) (model.py:84,87-88)
+    {
+      NormParams p{};
+      p.rows = T;
+      p.tok_ids = ids;
+      p.src = wptr<float>(e, "embed.tok");
+      p.ld_src = d;
+      p.w = wptr<float>(e, "embed.norm.w");
+      p.out_f32 = E.h;
+      p.ld_out_f32 = d;
+      if (fp8) {
+        p.out_fp8 = E.n8;
+        p.out_fp8_scale = E.n8s;
+      } else {
+        p.out_bf16 = E.n;
+      }
+      norm(p);
+    }
+    for (int i = 0; i < c.layers; ++i) {
+      const std::string pre = "enc." + std::to_string(i) + ".";
+      if (i > 0) {  // add_norm(h, pending, attn_norm): pending already added by Wo2's epilogue
+        NormParams p{};
+        p.rows = T;
+        p.src = E.h;
+        p.ld_src = d;
+        p.w = wptr<float>(e, pre + "attn_norm.w");
+        if (fp8) {
+          p.out_fp8 = E.n8;
+          p.out_fp8_scale = E.n8s;
+        } else {
+          p.out_bf16 = E.n;
+        }
+        norm(p);
+      }
+      gemm(E.wqkv[i], fp8 ? (const void*)E.n8 : (const void*)E.n, E.n8s, T, kEpiStore, E.qkv, 3 * d, nullptr, 0);
+      const bool glob = (i % c.global_every) == 0;
+      {
+        AttnParams a{};
+        a.qkv = E.qkv;
+        a.ld_qkv = 3 * d;
+        a.d = d;
+        a.s = s;
+        a.nq = s;
+        a.key_valid = valid;
+        a.cos = glob ? E.gcos : E.lcos;
+        a.sin = glob ? E.gsin : E.lsin;
+        a.window = glob ? -1 : c.local_window;
+        a.out = E.attn;
+        a.ld_out = d;
+        attention(a, b, c.heads);
+      }
+      if (fp8) {
+        QuantParams q{};
+        q.rows = T;
+        q.k = d;
+        q.src = E.attn;
+        q.q = E.a8;
+        q.scale = E.a8s;
+        count(launch_quant_fp8(q, st, pdl()), "quant launch");
+      }
+      gemm(E.wo[i], fp8 ? (const void*)E.a8 : (const void*)E.attn, E.a8s, T, kEpiResidual, nullptr, 0, E.h, d);
+      {
+        NormParams p{};
+        p.rows = T;
+        p.src = E.h;
+        p.ld_src = d;
+        p.w = wptr<float>(e, pre + "mlp_norm.w");
+        if (fp8) {
+          p.out_fp8 = E.n8;
+          p.out_fp8_scale = E.n8s;
+        } else {
+          p.out_bf16 = E.n;
+        }
+        norm(p);
+      }
+      gemm(E.wi[i], fp8 ? (const void*)E.n8 : (const void*)E.n, E.n8s, T, kEpiGeglu, E.g, I, nullptr, 0);
+      if (fp8) {
+        QuantParams q{};
+        q.rows = T;
+        q.k = I;
+        q.src = E.g;
+        q.q = E.g8;
+        q.scale = E.g8s;
+        count(launch_quant_fp8(q, st, pdl()), "quant launch");
+      }
+      gemm(E.wo2[i], fp8 ? (const void*)E.g8 : (const void*)E.g, E.g8s, T, kEpiResidual, nullptr, 0, E.h, d);
+    }
+    // final_norm(h + pending) + type_emb(qtype) (model.py:102-104), fused with
+    // the first head layer's norm1 (model.py:59).
+    {
+      NormParams p{};
+      p.rows = T;
+      p.src = E.h;
+      p.ld_src = d;
+      p.w = wptr<float>(e, "final_norm.w");
+      p.add_table = wptr<float>(e, "type_emb");
+      p.add_idx = qtype;
+      p.add_div = s;
+      p.out_f32 = E.h;
+      p.ld_out_f32 = d;
+      if (c.head_layers > 0) {
+        p.second_w = wptr<float>(e, "head.0.norm1.w");
+        p.second_b = wptr<float>(e, "head.0.norm1.b");
+        p.out_bf16 = E.n;
+      }
+      norm(p);
+    }
+    for (int j = 0; j < c.head_layers; ++j) {
+      const std::string pre = "head." + std::to_string(j) + ".";
+      const bool last = j == c.head_layers - 1;
+      if (j > 0) {
+        NormParams p{};
+        p.rows = T;
+        p.src = E.h;
+        p.ld_src = d;
+        p.w = wptr<float>(e, pre + "norm1.w");
+        p.b = wptr<float>(e, pre + "norm1.b");
+        p.out_bf16 = E.n;
+        norm(p);
+      }
+      gemm(E.in_proj[j], E.n, nullptr, T, kEpiStore, E.qkv, 3 * d, nullptr, 0);
+      AttnParams a{};
+      a.qkv = E.qkv;
+      a.ld_qkv = 3 * d;
+      a.d = d;
+      a.s = s;
+      a.key_valid = valid;
+      a.window = -1;
+      a.ld_out = d;
+      float* hrows = E.h;
+      int rows = T;
+      __nv_bfloat16* arows = E.attn;
+      __nv_bfloat16* nrows = E.n;
+      __nv_bfloat16* frows = E.g;
+      if (!last) {
+        a.nq = s;
+        a.out = E.attn;
+        attention(a, b, c.head_heads);
+      } else {  // only CLS and marker rows leave the last head layer (model.py:64-66)
+        a.nq = 1 + k;
+        a.q_pos = selpos;
+        a.out = E.asel;
+        attention(a, b, c.head_heads);
+        count(launch_gather_rows(E.hsel, E.h, selsrc, R, d, st, pdl()), "gather launch");
+        hrows = E.hsel;
+        rows = R;
+        arows = E.asel;
+        nrows = E.nsel;
+        frows = E.fsel;
+      }
+      gemm(E.out_proj[j], arows, nullptr, rows, kEpiResidual, nullptr, 0, hrows, d);
+      {
+        NormParams p{};
+        p.rows = rows;
+        p.src = hrows;
+        p.ld_src = d;
+        p.w = wptr<float>(e, pre + "norm2.w");
+        p.b = wptr<float>(e, pre + "norm2.b");
+        p.out_bf16 = nrows;
+        norm(p);
+      }
+      gemm(E.lin1[j], nrows, nullptr, rows, kEpiRelu, frows, F, nullptr, 0);
+      gemm(E.lin2[j], frows, nullptr, rows, kEpiResidual, nullptr, 0, hrows, d);
+    }
+    if (c.head_layers == 0)
+      count(launch_gather_rows(E.hsel, E.h, selsrc, R, d, st, pdl()), "gather launch");
+    // scorer: LN -> bf16 -> Linear -> GELU (model.py:113-114)
+    {
+      NormParams p{};
+      p.rows = BK;
+      p.src = E.hsel;
+      p.ld_src = d;
+      p.row_map = score_rows;
+      p.w = wptr<float>(e, "scorer.norm.w");
+      p.b = wptr<float>(e, "scorer.norm.b");
+      p.out_bf16 = E.msc;
+      norm(p);
+    }
+    gemm(E.sc_fc1, E.msc, nullptr, BK, kEpiGelu, E.zsc, d, nullptr, 0);
+    {
+      TailParams t{};
+      t.k = k;
+      t.d = d;
+      t.act_hidden = c.act_hidden;
+      t.z = E.zsc;
+      t.fc2_w = wptr<__nv_bfloat16>(e, "scorer.fc2.w");
+      t.fc2_b = wptr<__nv_bfloat16>(e, "scorer.fc2.b");
+      t.marker_mask = mmask;
+      t.h_sel = E.hsel;
+      t.a1_w = wptr<__nv_bfloat16>(e, "act.fc1.w");
+      t.a1_b = wptr<__nv_bfloat16>(e, "act.fc1.b");
+      t.a2_w = wptr<__nv_bfloat16>(e, "act.fc2.w");
+      t.a2_b = wptr<__nv_bfloat16>(e, "act.fc2.b");
+      t.logits = E.d_out;
+      t.act = E.d_out + (size_t)c.max_batch * c.max_options;
+      count(launch_tail(t, b, st, pdl()), "tail launch");
+    }
+  }
+};
+
+Proj make_proj(laya_b200_engine* e, const std::string& wname, const std::string& bname, int kind,
+               const void* qweights, const float* qscale) {
+  const ParamInfo& pi = e->params.at(wname);
+  Proj p;
+  p.N = pi.rows;
+  p.K = pi.cols;
+  p.kind = kind;
+  p.bias = bname.empty() ? nullptr : wptr<__nv_bfloat16>(e, bname);
+  if (kind == kKindBf16) {
+    p.w = e->warena + pi.offset;
+    p.map = make_map(p.w, p.N, p.K, 2, 128);
+  } else {
+    p.w = qweights;
+    p.w_scale = qscale;
+    p.map = make_map(p.w, p.N, p.K, 1, 128);
+  }
+  return p;
+}
+
+void free_slot(Slot& s) {
+  if (s.io_exec) cudaGraphExecDestroy(s.io_exec);
+  if (s.dev_exec) cudaGraphExecDestroy(s.dev_exec);
+  s = Slot{};
+}
+
+int guard(laya_b200_engine* e, const std::function<void()>& fn) {
+  try {
+    if (!e) fail("engine is NULL");
+    ck(cudaSetDevice(e->device), "cudaSetDevice");
+    fn();
+    e->last_error.clear();
+    return 0;
+  } catch (const Error& err) {
+    if (e) e->last_error = err.msg;
+    return 1;
+  } catch (const std::exception& ex) {
+    if (e) e->last_error = ex.what();
+    return 1;
+  }
+}
+
+}  // namespace
+
+extern "C" {
+
+int laya_b200_create(int device, const laya_b200_config* cfg, laya_b200_engine** out) {
+  if (!out || !cfg) {
+    g_create_error = "null argument";
+    return 1;
+  }
+  *out = nullptr;
+  std::unique_ptr<laya_b200_engine> e(new laya_b200_engine());
+  try {
+    validate_cfg(*cfg);
+    int n = 0;
+    ck(cudaGetDeviceCount(&n), "cudaGetDeviceCount");
+    if (device < 0 || device >= n) fail("device %d out of range (%d visible)", device, n);
+    e->device = device;
+    e->cfg = *cfg;
+    ck(cudaSetDevice(device), "cudaSetDevice");
+    cudaDeviceProp prop;
+    ck(cudaGetDeviceProperties(&prop, device), "cudaGetDeviceProperties");
+    if (prop.major != 10) fail("the b200 engine needs an sm_100 GPU; found %s (SM%d%d)", prop.name, prop.major, prop.minor);
+    e->sm_count = prop.multiProcessorCount;
+    ck(cudaStreamCreateWithFlags(&e->stream, cudaStreamNonBlocking), "stream");
+    ck(cudaEventCreate(&e->ev0), "event");
+    ck(cudaEventCreate(&e->ev1), "event");
+    // weights
+    size_t off = 0;
+    for (auto& t : param_table(*cfg)) {
+      ParamInfo pi{};
+      pi.rows = std::get<1>(t);
+      pi.cols = std::get<2>(t);
+      pi.dtype = std::get<3>(t);
+      pi.elems = (size_t)pi.rows * pi.cols;
+      pi.offset = off;
+      off = align_up(off + pi.elems * (pi.dtype == kF32 ? 4 : 2), 256);
+      e->params[std::get<0>(t)] = pi;
+    }
+    e->warena_bytes = off;
+    ck(cudaMalloc(&e->warena, off), "weight arena");
+    // activations
+    const laya_b200_config& c = *cfg;
+    const int d = c.hidden, I = c.intermediate, F = c.head_ff;
+    const size_t T = (size_t)c.max_batch * c.max_len;
+    const size_t R = (size_t)c.max_batch * (1 + c.max_options);
+    const size_t BK = (size_t)c.max_batch * c.max_options;
+    e->max_tokens = (int)T;
+    const size_t gw = (size_t)(I > F ? I : F);
+    std::vector<std::pair<void**, size_t>> bufs = {
+        {(void**)&e->h, T * d * 4},         {(void**)&e->n, T * d * 2},
+        {(void**)&e->qkv, T * 3 * d * 2},   {(void**)&e->attn, T * d * 2},
+        {(void**)&e->g, T * gw * 2},        {(void**)&e->n8, T * d},
+        {(void**)&e->a8, T * d},            {(void**)&e->g8, T * I},
+        {(void**)&e->n8s, T * 4},           {(void**)&e->a8s, T * 4},
+        {(void**)&e->g8s, T * 4},           {(void**)&e->hsel, R * d * 4},
+        {(void**)&e->asel, R * d * 2},      {(void**)&e->nsel, R * d * 2},
+        {(void**)&e->fsel, R * F * 2},      {(void**)&e->msc, BK * d * 2},
+        {(void**)&e->zsc, BK * d * 2},      {(void**)&e->gcos, (size_t)c.max_len * 64 * 4},
+        {(void**)&e->gsin, (size_t)c.max_len * 64 * 4}, {(void**)&e->lcos, (size_t)c.max_len * 64 * 4},
+        {(void**)&e->lsin, (size_t)c.max_len * 64 * 4},
+    };
+    size_t aoff = 0;
+    for (auto& b : bufs) aoff = align_up(aoff + b.second, 1024);
+    e->aarena_bytes = aoff;
+    ck(cudaMalloc(&e->aarena, aoff), "activation arena");
+    ck(cudaMemset(e->aarena, 0, aoff), "activation memset");
+    aoff = 0;
+    for (auto& b : bufs) {
+      *b.first = e->aarena + aoff;
+      aoff = align_up(aoff + b.second, 1024);
+    }
+    std::vector<float> cs, sn;
+    rope_tables(c.rope_theta_global, c.max_len, cs, sn);
+    ck(cudaMemcpy(e->gcos, cs.data(), cs.size() * 4, cudaMemcpyHostToDevice), "rope upload");
+    ck(cudaMemcpy(e->gsin, sn.data(), sn.size() * 4, cudaMemcpyHostToDevice), "rope upload");
+    rope_tables(c.rope_theta_local, c.max_len, cs, sn);
+    ck(cudaMemcpy(e->lcos, cs.data(), cs.size() * 4, cudaMemcpyHostToDevice), "rope upload");
+    ck(cudaMemcpy(e->lsin, sn.data(), sn.size() * 4, cudaMemcpyHostToDevice), "rope upload");
+    // I/O staging: int32 words [ids T | valid T | qtype B | mmask BK | selsrc R | selpos R | score BK]
+    e->off_ids = 0;
+    e->off_valid = T;
+    e->off_qtype = 2 * T;
+    e->off_mmask = e->off_qtype + c.max_batch;
+    e->off_selsrc = e->off_mmask + BK;
+    e->off_selpos = e->off_selsrc + R;
+    e->off_score = e->off_selpos + R;
+    e->in_words = e->off_score + BK;
+    e->out_words = BK + (size_t)c.max_batch * 2;
+    ck(cudaMalloc(&e->d_in, e->in_words * 4), "input buffer");
+    ck(cudaMemset(e->d_in, 0, e->in_words * 4), "input memset");
+    ck(cudaMalloc(&e->d_out, e->out_words * 4), "output buffer");
+    ck(cudaHostAlloc(&e->h_in, e->in_words * 4, cudaHostAllocDefault), "pinned input");
+    ck(cudaHostAlloc(&e->h_out, e->out_words * 4, cudaHostAllocDefault), "pinned output");
+    ck(cudaHostAlloc(&e->status_host, 64, cudaHostAllocMapped), "status word");
+    memset(e->status_host, 0, 64);
+    ck(cudaHostGetDevicePointer((void**)&e->status_dev, e->status_host, 0), "status pointer");
+    if (!get_encode_fn()) fail("cuTensorMapEncodeTiled is unavailable");
+  } catch (const Error& err) {
+    g_create_error = err.msg;
+    laya_b200_destroy(e.release());
+    return 1;
+  }
+  *out = e.release();
+  return 0;
+}
+
+int laya_b200_set_weight(laya_b200_engine* e, const char* name, const void* host, size_t bytes) {
+  return guard(e, [&] {
+    if (!name || !host) fail("null argument");
+    if (e->finalized) fail("weights are already finalized");
+    auto it = e->params.find(name);
+    if (it == e->params.end()) fail("unknown parameter %s", name);
+    ParamInfo& pi = it->second;
+    const size_t want = pi.elems * (pi.dtype == kF32 ? 4 : 2);
+    if (bytes != want) fail("parameter %s: expected %zu bytes, got %zu", name, want, bytes);
+    uint8_t* dst = e->warena + pi.offset;
+    const std::string n(name);
+    const bool is_wi = n.size() > 3 && n.compare(n.size() - 3, 3, ".wi") == 0 && n.rfind("enc.", 0) == 0;
+    if (is_wi) {
+      // Interleave act/gate rows in blocks of 64 so that each 128-row GEMM
+      // tile holds act rows j and their gate rows j+64 (GEGLU epilogue).
+      const int I = e->cfg.intermediate, K = pi.cols;
+      const size_t rowb = (size_t)K * 2;
+      const uint8_t* src = static_cast<const uint8_t*>(host);
+      for (int t = 0; t < I / 64; ++t) {
+        ck(cudaMemcpy(dst + (size_t)(128 * t) * rowb, src + (size_t)(64 * t) * rowb, 64 * rowb,
+                      cudaMemcpyHostToDevice),
+           "weight upload");
+        ck(cudaMemcpy(dst + (size_t)(128 * t + 64) * rowb, src + (size_t)(I + 64 * t) * rowb, 64 * rowb,
+                      cudaMemcpyHostToDevice),
+           "weight upload");
+      }
+    } else {
+      ck(cudaMemcpy(dst, host, bytes, cudaMemcpyHostToDevice), "weight upload");
+    }
+    pi.uploaded = true;
+  });
+}
+
+int laya_b200_finalize(laya_b200_engine* e, int precision) {
+  return guard(e, [&] {
+    if (e->finalized) fail("already finalized");
+    for (auto& kv : e->params)
+      if (!kv.second.uploaded) fail("parameter %s was not uploaded", kv.first.c_str());
+    if (precision != LAYA_B200_BF16 && precision != LAYA_B200_FP8)
+      fail("precision %d is not available in this build", precision);
+    const laya_b200_config& c = e->cfg;
+    const int kind = precision == LAYA_B200_FP8 ? kKindFp8 : kKindBf16;
+    std::vector<std::pair<std::string, size_t>> qoff;  // weight name -> offset of e4m3 bytes, scales follow
+    if (kind == kKindFp8) {
+      size_t off = 0;
+      for (int i = 0; i < c.layers; ++i)
+        for (const char* nm : {"wqkv", "wo", "wi", "wo2"}) {
+          const std::string name = "enc." + std::to_string(i) + "." + nm;
+          const ParamInfo& pi = e->params.at(name);
+          qoff.emplace_back(name, off);
+          off = align_up(off + pi.elems, 256);
+          off = align_up(off + (size_t)pi.rows * 4, 256);
+        }
+      e->qarena_bytes = off;
+      ck(cudaMalloc(&e->qarena, off), "packed weight arena");
+      for (auto& q : qoff) {
+        const ParamInfo& pi = e->params.at(q.first);
+        uint8_t* wq = e->qarena + q.second;
+        float* ws = reinterpret_cast<float*>(e->qarena + align_up(q.second + pi.elems, 256));
+        ck(launch_pack_fp8_rows(reinterpret_cast<const __nv_bfloat16*>(e->warena + pi.offset), wq, ws, pi.rows,
+                                pi.cols, e->stream),
+           "fp8 packer");
+      }
+      ck(cudaStreamSynchronize(e->stream), "fp8 packer");
+    }
+    auto enc_proj = [&](const std::string& name) {
+      if (kind == kKindBf16) return make_proj(e, name, "", kKindBf16, nullptr, nullptr);
+      for (auto& q : qoff)
+        if (q.first == name) {
+          const ParamInfo& pi = e->params.at(name);
+          return make_proj(e, name, "", kKindFp8, e->qarena + q.second,
+                           reinterpret_cast<const float*>(e->qarena + align_up(q.second + pi.elems, 256)));
+        }
+      fail("no packed weights for %s", name.c_str());
+    };
+    for (int i = 0; i < c.layers; ++i) {
+      const std::string p = "enc." + std::to_string(i) + ".";
+      e->wqkv.push_back(enc_proj(p + "wqkv"));
+      e->wo.push_back(enc_proj(p + "wo"));
+      e->wi.push_back(enc_proj(p + "wi"));
+      e->wo2.push_back(enc_proj(p + "wo2"));
+    }
+    for (int j = 0; j < c.head_layers; ++j) {
+      const std::string p = "head." + std::to_string(j) + ".";
+      e->in_proj.push_back(make_proj(e, p + "in_proj.w", p + "in_proj.b", kKindBf16, nullptr, nullptr));
+      e->out_proj.push_back(make_proj(e, p + "out_proj.w", p + "out_proj.b", kKindBf16, nullptr, nullptr));
+      e->lin1.push_back(make_proj(e, p + "linear1.w", p + "linear1.b", kKindBf16, nullptr, nullptr));
+      e->lin2.push_back(make_proj(e, p + "linear2.w", p + "linear2.b", kKindBf16, nullptr, nullptr));
+    }
+    e->sc_fc1 = make_proj(e, "scorer.fc1.w", "scorer.fc1.b", kKindBf16, nullptr, nullptr);
+    e->precision = precision;
+    e->finalized = true;
+  });
+}
+
+int laya_b200_capture(laya_b200_engine* e, int batch, int seq, int options, int unmasked, int* slot) {
+  return guard(e, [&] {
+    if (!e->finalized) fail("finalize the weights before capturing");
+    if (!slot) fail("null slot pointer");
+    const laya_b200_config& c = e->cfg;
+    if (batch < 1 || batch > c.max_batch) fail("batch %d outside [1, %d]", batch, c.max_batch);
+    if (seq < 1 || seq > c.max_len) fail("seq %d outside [1, %d]", seq, c.max_len);
+    if (options < 2 || options > c.max_options) fail("options %d outside [2, %d]", options, c.max_options);
+    Slot s;
+    s.sh = Shape{batch, seq, options, unmasked ? 1 : 0};
+    for (int variant = 0; variant < 2; ++variant) {
+      cudaGraph_t graph = nullptr;
+      ck(cudaStreamBeginCapture(e->stream, cudaStreamCaptureModeThreadLocal), "begin capture");
+      try {
+        if (variant == 0)
+          ck(cudaMemcpyAsync(e->d_in, e->h_in, e->in_words * 4, cudaMemcpyHostToDevice, e->stream), "H2D");
+        e->launches = 0;
+        Fwd f{e, e->stream};
+        f.run(s.sh);
+        s.kernels = e->launches;
+        if (variant == 0)
+          ck(cudaMemcpyAsync(e->h_out, e->d_out, e->out_words * 4, cudaMemcpyDeviceToHost, e->stream), "D2H");
+      } catch (...) {
+        cudaStreamEndCapture(e->stream, &graph);
+        if (graph) cudaGraphDestroy(graph);
+        throw;
+      }
+      ck(cudaStreamEndCapture(e->stream, &graph), "end capture");
+      cudaGraphExec_t exec = nullptr;
+      cudaError_t err = cudaGraphInstantiate(&exec, graph, 0);
+      cudaGraphDestroy(graph);
+      ck(err, "graph instantiate");
+      (variant == 0 ? s.io_exec : s.dev_exec) = exec;
+    }
+    s.live = true;
+    for (size_t i = 0; i < e->slots.size(); ++i)
+      if (!e->slots[i].live) {
+        e->slots[i] = s;
+        *slot = (int)i;
+        return;
+      }
+    e->slots.push_back(s);
+    *slot = (int)e->slots.size() - 1;
+  });
+}
+
+int laya_b200_release(laya_b200_engine* e, int slot) {
+  return guard(e, [&] {
+    if (slot < 0 || slot >= (int)e->slots.size() || !e->slots[slot].live) fail("no slot %d", slot);
+    ck(cudaStreamSynchronize(e->stream), "sync");
+    free_slot(e->slots[slot]);
+  });
+}
+
+int laya_b200_run(laya_b200_engine* e, int slot, const int64_t* input_ids, const int64_t* attention_mask,
+                  const int64_t* marker_pos, const uint8_t* marker_mask, const int64_t* qtype, float* logits,
+                  float* act) {
+  return guard(e, [&] {
+    if (slot < 0 || slot >= (int)e->slots.size() || !e->slots[slot].live) fail("no slot %d", slot);
+    if (!input_ids || !attention_mask || !marker_pos || !marker_mask || !qtype || !logits || !act)
+      fail("null buffer");
+    const Slot& sl = e->slots[slot];
+    const int b = sl.sh.b, s = sl.sh.s, k = sl.sh.k;
+    const laya_b200_config& c = e->cfg;
+    int32_t* w = e->h_in;
+    // Pack and validate on the host; nothing out of range reaches a kernel.
+    for (int i = 0; i < b * s; ++i) {
+      const int64_t id = input_ids[i];
+      if (id < 0 || id >= c.vocab) fail("input_ids[%d]=%lld outside [0, %d)", i, (long long)id, c.vocab);
+      w[e->off_ids + i] = (int32_t)id;
+      w[e->off_valid + i] = attention_mask[i] != 0;
+    }
+    for (int q = 0; q < b; ++q) {
+      if (qtype[q] < 0 || qtype[q] >= c.num_qtypes) fail("qtype[%d]=%lld out of range", q, (long long)qtype[q]);
+      w[e->off_qtype + q] = (int32_t)qtype[q];
+      w[e->off_selsrc + q * (1 + k)] = q * s;
+      w[e->off_selpos + q * (1 + k)] = 0;
+      for (int j = 0; j < k; ++j) {
+        const int64_t pos = marker_pos[q * k + j];
+        if (pos < 0 || pos >= s) fail("marker_pos[%d][%d]=%lld outside [0, %d)", q, j, (long long)pos, s);
+        w[e->off_mmask + q * k + j] = marker_mask[q * k + j] != 0;
+        w[e->off_selsrc + q * (1 + k) + 1 + j] = q * s + (int32_t)pos;
+        w[e->off_selpos + q * (1 + k) + 1 + j] = (int32_t)pos;
+        w[e->off_score + q * k + j] = q * (1 + k) + 1 + j;
+      }
+    }
+    ck(cudaGraphLaunch(sl.io_exec, e->stream), "graph launch");
+    ck(cudaStreamSynchronize(e->stream), "forward");
+    const uint32_t st = __atomic_load_n(e->status_host, __ATOMIC_ACQUIRE);
+    if (st) {
+      e->status_host[0] = 0;
+      fail("a device-side wait timed out (status %u); the results of this call are invalid", st);
+    }
+    memcpy(logits, e->h_out, sizeof(float) * b * k);
+    memcpy(act, e->h_out + (size_t)c.max_batch * c.max_options, sizeof(float) * b * 2);
+  });
+}
+
+int laya_b200_replay_device(laya_b200_engine* e, int slot, int iterations, float* ms) {
+  return guard(e, [&] {
+    if (slot < 0 || slot >= (int)e->slots.size() || !e->slots[slot].live) fail("no slot %d", slot);
+    if (iterations < 1 || !ms) fail("bad arguments");
+    const Slot& sl = e->slots[slot];
+    ck(cudaEventRecord(e->ev0, e->stream), "event");
+    for (int i = 0; i < iterations; ++i) ck(cudaGraphLaunch(sl.dev_exec, e->stream), "graph launch");
+    ck(cudaEventRecord(e->ev1, e->stream), "event");
+    ck(cudaEventSynchronize(e->ev1), "replay");
+    float t = 0.f;
+    ck(cudaEventElapsedTime(&t, e->ev0, e->ev1), "elapsed");
+    if (e->status_host[0]) {
+      e->status_host[0] = 0;
+      fail("a device-side wait timed out during replay");
+    }
+    *ms = t / iterations;
+  });
+}
+
+int laya_b200_kernel_count(laya_b200_engine* e, int slot, int* count) {
+  return guard(e, [&] {
+    if (slot < 0 || slot >= (int)e->slots.size() || !e->slots[slot].live || !count) fail("no slot %d", slot);
+    *count = e->slots[slot].kernels;
+  });
+}
+
+int laya_b200_read_buffer(laya_b200_engine* e, const char* name, void* dst, size_t bytes) {
+  return guard(e, [&] {
+    if (!name || !dst) fail("null argument");
+    const laya_b200_config& c = e->cfg;
+    const size_t T = (size_t)c.max_batch * c.max_len, d = c.hidden;
+    const size_t R = (size_t)c.max_batch * (1 + c.max_options), BK = (size_t)c.max_batch * c.max_options;
+    const std::string n(name);
+    const void* src = nullptr;
+    size_t cap = 0;
+    if (n == "h") { src = e->h; cap = T * d * 4; }
+    else if (n == "n") { src = e->n; cap = T * d * 2; }
+    else if (n == "qkv") { src = e->qkv; cap = T * 3 * d * 2; }
+    else if (n == "attn") { src = e->attn; cap = T * d * 2; }
+    else if (n == "g") { src = e->g; cap = T * (size_t)(c.intermediate > c.head_ff ? c.intermediate : c.head_ff) * 2; }
+    else if (n == "hsel") { src = e->hsel; cap = R * d * 4; }
+    else if (n == "msc") { src = e->msc; cap = BK * d * 2; }
+    else if (n == "zsc") { src = e->zsc; cap = BK * d * 2; }
+    else fail("unknown buffer %s", name);
+    if (bytes > cap) fail("buffer %s holds %zu bytes, %zu requested", name, cap, bytes);
+    ck(cudaStreamSynchronize(e->stream), "sync");
+    ck(cudaMemcpy(dst, src, bytes, cudaMemcpyDeviceToHost), "read buffer");
+  });
+}
+
+const char* laya_b200_last_error(laya_b200_engine* e) {
+  return e ? e->last_error.c_str() : g_create_error.c_str();
+}
+
+int laya_b200_destroy(laya_b200_engine* e) {
+  if (!e) return 0;
+  cudaSetDevice(e->device);
+  if (e->stream) cudaStreamSynchronize(e->stream);
+  for (auto& s : e->slots) free_slot(s);
+  cudaFree(e->warena);
+  cudaFree(e->qarena);
+  cudaFree(e->aarena);
+  cudaFree(e->d_in);
+  cudaFree(e->d_out);
+  if (e->h_in) cudaFreeHost(e->h_in);
+  if (e->h_out) cudaFreeHost(e->h_out);
+  if (e->status_host) cudaFreeHost(e->status_host);
+  if (e->ev0) cudaEventDestroy(e->ev0);
+  if (e->ev1) cudaEventDestroy(e->ev1);
+  if (e->stream) cudaStreamDestroy(e->stream);
+  delete e;
+  return 0;
+}
+
+}  // extern "C"

@@ -1,0 +1,350 @@
+// Projection GEMM for every Linear of the Laya forward, on tcgen05 tensor
+// cores.  Replaces the reference's cuBLAS / Triton / torch._scaled_mm calls
+// (src/laya_blackwell/model.py:91,97,100-101,64-69,114;
+//  src/laya_blackwell/quantization.py:88-101).
+//
+// Orientation ("swap AB"): out[m][n] = sum_k X[m][k] * W[n][k].  The weight
+// tile (128 rows of W) is the MMA's A operand and sits on the 128 TMEM lanes;
+// the token tile (BN rows of X) is the MMA's N dimension.  At batch 1 the
+// token count is 64, so the 128-wide MMA M axis is always full.
+//
+// Pipeline per CTA: thread 0 issues TMA loads (weights first, before the
+// programmatic-dependent-launch wait, because weights never depend on the
+// previous kernel), thread 32 issues tcgen05.mma into a TMEM accumulator,
+// then all 128 threads move the accumulator to shared memory.
+//
+// Split-K: a thread-block cluster of S CTAs shares one output tile, each CTA
+// reducing a slice of K.  After the MMAs every CTA parks its fp32 partial in
+// its own shared memory; CTA r then sums rows {j, j+64 : j in its share} over
+// all S partials through distributed shared memory in rank order 0..S-1, so
+// the result is deterministic and no global workspace is needed.  The same
+// pairing of row j with row j+64 lets the GEGLU epilogue see act and gate of
+// one output column together (the packer interleaves Wi in blocks of 64).
+#include "common.cuh"
+#include "params.h"
+#include "launch.h"
+
+#include <cstdio>
+#include <mutex>
+
+namespace laya {
+
+template <int BN, int KIND, int STAGES>
+struct GemmCfg {
+  static constexpr int A_BYTES = 128 * 128;   // 128 weight rows x 128 bytes of K
+  static constexpr int B_BYTES = BN * 128;    // BN token rows x 128 bytes of K
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr int PIPE_BYTES = STAGES * STAGE_BYTES;
+  static constexpr int PART_BYTES = BN * 128 * 4;
+  static constexpr int MAIN_BYTES = PIPE_BYTES > PART_BYTES ? PIPE_BYTES : PART_BYTES;
+  static constexpr int BAR_BYTES = 256;
+  static constexpr int SMEM = MAIN_BYTES + BAR_BYTES + 1024;
+  static constexpr int TMEM_COLS = BN < 32 ? 32 : BN;
+  static constexpr int K_ELEMS = KIND == kKindBf16 ? 64 : 128;
+};
+
+template <int KIND>
+DEVI void epilogue_pair(const GemmParams& p, int m, int n_lo, int geglu_col, float lo, float hi) {
+  const int n_hi = n_lo + 64;
+  if (KIND == kKindFp8) {
+    const float sa = p.a_scale[m];
+    lo = (lo * sa) * p.w_scale[n_lo];
+    hi = (hi * sa) * p.w_scale[n_hi];
+  } else if (KIND == kKindNvfp4) {
+    const float sa = p.a_scale[m] * p.w_tensor_scale;
+    lo *= sa;
+    hi *= sa;
+  }
+  switch (p.epilogue) {
+    case kEpiGeglu: {
+      const float a = bf16_round(lo), g = bf16_round(hi);
+      const float ge = bf16_round(gelu_erf(a));
+      p.out[(size_t)m * p.ldo + geglu_col] = __float2bfloat16_rn(ge * g);
+      break;
+    }
+    case kEpiResidual: {
+      if (p.bias) {
+        lo += __bfloat162float(p.bias[n_lo]);
+        hi += __bfloat162float(p.bias[n_hi]);
+      }
+      float* r = p.resid + (size_t)m * p.ldr;
+      r[n_lo] = r[n_lo] + bf16_round(lo);
+      r[n_hi] = r[n_hi] + bf16_round(hi);
+      break;
+    }
+    default: {
+      if (p.bias) {
+        lo += __bfloat162float(p.bias[n_lo]);
+        hi += __bfloat162float(p.bias[n_hi]);
+      }
+      if (p.epilogue == kEpiRelu) {
+        lo = fmaxf(lo, 0.f);
+        hi = fmaxf(hi, 0.f);
+      } else if (p.epilogue == kEpiGelu) {
+        lo = gelu_erf(bf16_round(lo));
+        hi = gelu_erf(bf16_round(hi));
+      }
+      __nv_bfloat16* o = p.out + (size_t)m * p.ldo;
+      o[n_lo] = __float2bfloat16_rn(lo);
+      o[n_hi] = __float2bfloat16_rn(hi);
+      break;
+    }
+  }
+}
+
+template <int BN, int KIND, int STAGES>
+__global__ void __launch_bounds__(128, 1)
+    gemm_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ CUtensorMap xmap,
+                const GemmParams p) {
+  using C = GemmCfg<BN, KIND, STAGES>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + STAGES * C::A_BYTES;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::MAIN_BYTES);
+  uint64_t* empty = full + STAGES;
+  uint64_t* done = empty + STAGES;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
+  uint32_t* failed = tmem_slot + 1;
+
+  const int tid = threadIdx.x, warp = tid >> 5;
+  const int tile_n = blockIdx.x, tile_m = blockIdx.y;
+  const int split = gridDim.z, rank = blockIdx.z;
+  const int kb0 = (int)((long long)rank * p.kblocks / split);
+  const int kb1 = (int)((long long)(rank + 1) * p.kblocks / split);
+  const int nkb = kb1 - kb0;
+
+  griddep_launch_dependents();
+
+  if (tid == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(done, 1);
+    *failed = 0;
+    fence_mbar_init();
+    prefetch_tensormap(&wmap);
+    prefetch_tensormap(&xmap);
+  }
+  if (warp == 0) {
+    tmem_alloc(tmem_slot, C::TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  int issued = 0;  // producer: loads issued (for the drain on failure)
+  if (tid == 0) {
+    const uint64_t pol_w = policy_evict_first();
+    const uint64_t pol_x = policy_evict_last();
+    const int pre = nkb < STAGES ? nkb : STAGES;
+    for (int i = 0; i < pre; ++i) {
+      mbar_expect_tx(&full[i], C::STAGE_BYTES);
+      tma_load_2d(sA + i * C::A_BYTES, &wmap, &full[i], (kb0 + i) * C::K_ELEMS, tile_n * 128, pol_w);
+    }
+    griddep_wait();
+    for (int i = 0; i < pre; ++i)
+      tma_load_2d(sB + i * C::B_BYTES, &xmap, &full[i], (kb0 + i) * C::K_ELEMS, tile_m * BN, pol_x);
+    issued = pre;
+    for (int i = pre; i < nkb; ++i) {
+      const int s = i % STAGES;
+      if (!mbar_wait(&empty[s], ((i / STAGES) - 1) & 1)) {
+        record_status(p.status, kStatusGemmEmptyTimeout);
+        atomicExch(failed, 1u);
+        break;
+      }
+      mbar_expect_tx(&full[s], C::STAGE_BYTES);
+      tma_load_2d(sA + s * C::A_BYTES, &wmap, &full[s], (kb0 + i) * C::K_ELEMS, tile_n * 128, pol_w);
+      tma_load_2d(sB + s * C::B_BYTES, &xmap, &full[s], (kb0 + i) * C::K_ELEMS, tile_m * BN, pol_x);
+      issued = i + 1;
+    }
+  } else if (tid == 32) {
+    const uint32_t idesc = KIND == kKindBf16 ? idesc_bf16(128, BN) : idesc_e4m3(128, BN);
+    for (int i = 0; i < nkb; ++i) {
+      const int s = i % STAGES;
+      if (!mbar_wait(&full[s], (i / STAGES) & 1)) {
+        record_status(p.status, kStatusGemmFullTimeout);
+        atomicExch(failed, 1u);
+        break;
+      }
+      tc_fence_after();
+      const uint64_t ad = sw128_desc(smem_u32(sA + s * C::A_BYTES));
+      const uint64_t bd = sw128_desc(smem_u32(sB + s * C::B_BYTES));
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {  // 4 MMAs of 32 bytes of K each; +2 = 32 bytes in the descriptor
+        if (KIND == kKindBf16)
+          umma_f16(tmem, ad + 2 * k, bd + 2 * k, idesc, (i | k) != 0);
+        else
+          umma_f8(tmem, ad + 2 * k, bd + 2 * k, idesc, (i | k) != 0);
+      }
+      umma_commit(&empty[s]);
+    }
+    umma_commit(done);
+  }
+  __syncwarp();
+
+  // ---- epilogue: TMEM -> shared partial [BN][128] fp32
+  griddep_wait();
+  if (!mbar_wait(done, 0)) {
+    record_status(p.status, kStatusGemmDoneTimeout);
+    atomicExch(failed, 1u);
+  }
+  tc_fence_after();
+  float* part = reinterpret_cast<float*>(smem);
+  const uint32_t lane_addr = tmem + ((uint32_t)(warp * 32) << 16);
+  if (BN >= 32) {
+#pragma unroll 1
+    for (int c = 0; c < BN; c += 32) {
+      uint32_t r[32];
+      tmem_ld32(lane_addr + c, r);
+      tmem_wait_ld();
+#pragma unroll
+      for (int j = 0; j < 32; ++j) part[(c + j) * 128 + tid] = __uint_as_float(r[j]);
+    }
+  } else {
+    uint32_t r[16];
+    tmem_ld16(lane_addr, r);
+    tmem_wait_ld();
+#pragma unroll
+    for (int j = 0; j < 16; ++j) part[j * 128 + tid] = __uint_as_float(r[j]);
+  }
+  tc_fence_before();
+  if (split > 1)
+    cluster_sync_all();
+  else
+    __syncthreads();
+
+  // ---- reduction over the cluster and the epilogue
+  const int j0 = rank * 64 / split, j1 = (rank + 1) * 64 / split, np = j1 - j0;
+  const uint32_t part_addr = smem_u32(part);
+  for (int idx = tid; idx < np * BN; idx += 128) {
+    const int jj = j0 + idx % np;
+    const int ml = idx / np;
+    const int m = tile_m * BN + ml;
+    if (m >= p.M) continue;
+    const int off = ml * 128 + jj;
+    float lo, hi;
+    if (split == 1) {
+      lo = part[off];
+      hi = part[off + 64];
+    } else {
+      lo = 0.f;
+      hi = 0.f;
+      for (int q = 0; q < split; ++q) {
+        const uint32_t base = mapa_shared(part_addr, (uint32_t)q);
+        lo += ld_dsmem_f32(base + off * 4);
+        hi += ld_dsmem_f32(base + (off + 64) * 4);
+      }
+    }
+    epilogue_pair<KIND>(p, m, tile_n * 128 + jj, tile_n * 64 + jj, lo, hi);
+  }
+  if (split > 1) cluster_sync_all();
+
+  // ---- teardown: drain copies still in flight after a failure, free TMEM
+  if (tid == 0 && *failed) {
+    for (int i = (issued > STAGES ? issued - STAGES : 0); i < issued; ++i)
+      mbar_wait(&full[i % STAGES], (i / STAGES) & 1);
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) tmem_dealloc(tmem, C::TMEM_COLS);
+}
+
+// ------------------------------------------------------------------ host side
+
+namespace {
+
+template <int BN, int KIND, int STAGES>
+cudaError_t launch_one(const CUtensorMap& wmap, const CUtensorMap& xmap, const GemmParams& p, int tiles_n,
+                       int tiles_m, int split, cudaStream_t stream, bool pdl) {
+  using C = GemmCfg<BN, KIND, STAGES>;
+  auto kern = gemm_kernel<BN, KIND, STAGES>;
+  // Function attributes are per device: set them once for each device used.
+  static std::mutex mu;
+  static uint64_t ready = 0;
+  int dev = 0;
+  cudaError_t err = cudaGetDevice(&dev);
+  if (err != cudaSuccess) return err;
+  {
+    std::lock_guard<std::mutex> lock(mu);
+    if (!(ready >> dev & 1)) {
+      err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
+      if (err == cudaSuccess) err = cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+      if (err != cudaSuccess) return err;
+      ready |= uint64_t(1) << dev;
+    }
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(tiles_n, tiles_m, split);
+  cfg.blockDim = dim3(128, 1, 1);
+  cfg.dynamicSmemBytes = C::SMEM;
+  cfg.stream = stream;
+  cudaLaunchAttribute attrs[2];
+  int na = 0;
+  if (pdl) {
+    attrs[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attrs[na].val.programmaticStreamSerializationAllowed = 1;
+    ++na;
+  }
+  if (split > 1) {
+    attrs[na].id = cudaLaunchAttributeClusterDimension;
+    attrs[na].val.clusterDim.x = 1;
+    attrs[na].val.clusterDim.y = 1;
+    attrs[na].val.clusterDim.z = split;
+    ++na;
+  }
+  cfg.attrs = attrs;
+  cfg.numAttrs = na;
+  return cudaLaunchKernelEx(&cfg, kern, wmap, xmap, p);
+}
+
+template <int KIND>
+cudaError_t dispatch_bn(int bn, const CUtensorMap& wmap, const CUtensorMap& xmap, const GemmParams& p, int tn,
+                        int tm, int split, cudaStream_t st, bool pdl) {
+  switch (bn) {
+    case 16: return launch_one<16, KIND, 4>(wmap, xmap, p, tn, tm, split, st, pdl);
+    case 32: return launch_one<32, KIND, 4>(wmap, xmap, p, tn, tm, split, st, pdl);
+    case 64: return launch_one<64, KIND, 4>(wmap, xmap, p, tn, tm, split, st, pdl);
+    case 128: return launch_one<128, KIND, 3>(wmap, xmap, p, tn, tm, split, st, pdl);
+    case 256: return launch_one<256, KIND, 4>(wmap, xmap, p, tn, tm, split, st, pdl);
+  }
+  return cudaErrorInvalidValue;
+}
+
+}  // namespace
+
+int gemm_token_tile(int M) {
+  if (M <= 16) return 16;
+  if (M <= 32) return 32;
+  if (M <= 64) return 64;
+  if (M <= 128) return 128;
+  return 256;
+}
+
+int gemm_k_elems(int kind) { return kind == kKindBf16 ? 64 : 128; }
+
+// Split-K factor: fill about one wave of the 148 SMs with CTAs when the tile
+// grid alone is too small, at least two K blocks per CTA when possible.
+int gemm_split(int tiles, int kblocks, int sm_count, int max_split) {
+  if (tiles >= sm_count) return 1;
+  int s = sm_count / tiles;
+  if (s > max_split) s = max_split;
+  if (s > kblocks) s = kblocks;
+  if (s < 1) s = 1;
+  return s;
+}
+
+cudaError_t launch_gemm(int kind, const CUtensorMap& wmap, const CUtensorMap& xmap, const GemmParams& p, int bn,
+                        int split, cudaStream_t stream, bool pdl) {
+  const int tiles_n = p.N / 128;
+  const int tiles_m = (p.M + bn - 1) / bn;
+  if (p.N % 128 || split < 1 || split > 16 || split > p.kblocks) return cudaErrorInvalidValue;
+  if (kind == kKindBf16) return dispatch_bn<kKindBf16>(bn, wmap, xmap, p, tiles_n, tiles_m, split, stream, pdl);
+  if (kind == kKindFp8) return dispatch_bn<kKindFp8>(bn, wmap, xmap, p, tiles_n, tiles_m, split, stream, pdl);
+  return cudaErrorInvalidValue;
+}
+
+}  // namespace laya

@@ -1,0 +1,27 @@
+// Host-side launchers of the b200 kernels (all take the stream to enqueue on
+// and whether to allow programmatic dependent launch on the previous kernel).
+#pragma once
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include "params.h"
+
+namespace laya {
+
+int gemm_token_tile(int M);
+int gemm_k_elems(int kind);
+int gemm_split(int tiles, int kblocks, int sm_count, int max_split);
+cudaError_t launch_gemm(int kind, const CUtensorMap& wmap, const CUtensorMap& xmap, const GemmParams& p, int bn,
+                        int split, cudaStream_t stream, bool pdl);
+cudaError_t launch_gemm_nvfp4(const CUtensorMap& wmap, const CUtensorMap& xmap, const CUtensorMap& wsf,
+                              const CUtensorMap& xsf, const GemmParams& p, int bn, int split, cudaStream_t stream,
+                              bool pdl);
+cudaError_t launch_attention(const AttnParams& p, int batch, int heads, cudaStream_t stream, bool pdl);
+cudaError_t launch_norm(const NormParams& p, cudaStream_t stream, bool pdl);
+cudaError_t launch_quant_fp8(const QuantParams& p, cudaStream_t stream, bool pdl);
+cudaError_t launch_gather_rows(float* dst, const float* src, const int* map, int rows, int d, cudaStream_t stream,
+                               bool pdl);
+cudaError_t launch_tail(const TailParams& p, int batch, cudaStream_t stream, bool pdl);
+cudaError_t launch_pack_fp8_rows(const __nv_bfloat16* w, uint8_t* q, float* scale, int rows, int k,
+                                 cudaStream_t stream);
+
+}  // namespace laya

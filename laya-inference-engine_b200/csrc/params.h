@@ -1,0 +1,107 @@
+// Kernel parameter blocks shared by the host runtime and the kernels.
+#pragma once
+#include <stdint.h>
+#include <cuda_bf16.h>
+
+namespace laya {
+
+// Epilogues of the projection GEMM.  v is the fp32 accumulator after the
+// precision's scales; every bf16() is a round-to-nearest-even to bf16.
+enum GemmEpilogue : int {
+  kEpiStore = 0,     // out[m][n] = bf16(v + bias[n])
+  kEpiRelu = 1,      // out[m][n] = bf16(relu(v + bias[n]))
+  kEpiGelu = 2,      // out[m][n] = bf16(gelu(bf16(v + bias[n])))
+  kEpiGeglu = 3,     // tile rows 0-63 act, 64-127 gate: out[m][j] = bf16(bf16(gelu(bf16(act))) * bf16(gate))
+  kEpiResidual = 4,  // resid[m][n] += bf16(v + bias[n])   (fp32 residual stream)
+};
+
+enum GemmKind : int { kKindBf16 = 0, kKindFp8 = 1, kKindNvfp4 = 2 };
+
+struct GemmParams {
+  int M;          // token rows
+  int N;          // weight rows (features) -- multiple of 128
+  int K;          // reduction length in elements
+  int kblocks;    // number of K blocks
+  int epilogue;   // GemmEpilogue
+  __nv_bfloat16* out;       // bf16 output [M][ldo]
+  int ldo;
+  float* resid;             // fp32 residual [M][ldr] (kEpiResidual)
+  int ldr;
+  const __nv_bfloat16* bias;  // [N] or null
+  const float* a_scale;     // fp8/nvfp4: per-token fp32 scale [M]
+  const float* w_scale;     // fp8: per-feature fp32 scale [N]
+  float w_tensor_scale;     // nvfp4: weight tensor scale
+  uint32_t* status;         // device-visible status word
+};
+
+struct NormParams {
+  int rows;
+  int d;
+  float eps;
+  // Source rows: embedding table gathered by token id, or an fp32 matrix
+  // (optionally through a row map).
+  const int* tok_ids;       // [rows] or null
+  const float* src;         // fp32 [*, ld_src] (table when tok_ids != null)
+  int ld_src;
+  const int* row_map;       // [rows] source row per output row, or null
+  const float* w;           // LayerNorm weight [d]
+  const float* b;           // LayerNorm bias [d] or null
+  // y = LN(x) * w + b (+ add_table[add_idx[row / add_div]])
+  const float* add_table;   // [*, d] or null
+  const int* add_idx;
+  int add_div;
+  float* out_f32;           // y (fp32) or null; may alias src (in place)
+  int ld_out_f32;
+  // bf16 output: bf16(y) when second_w == null; otherwise bf16(LN2(y)) with
+  // second_w / second_b (a second LayerNorm fused on the same row).
+  const float* second_w;
+  const float* second_b;
+  int raw_bf16;             // 1: bf16 output is bf16(x) of the *input* row (encoder layer 0 input)
+  __nv_bfloat16* out_bf16;  // [rows][d] or null
+  uint8_t* out_fp8;         // e4m3 per-row quantisation of the bf16 output, or null
+  float* out_fp8_scale;     // [rows]
+};
+
+struct AttnParams {
+  const __nv_bfloat16* qkv;  // [tokens][ld_qkv]; q at col h*64, k at d + h*64, v at 2d + h*64
+  int ld_qkv;
+  int d;                     // heads * 64
+  int s;                     // keys per sequence
+  int nq;                    // queries per sequence
+  const int* q_pos;          // [b][nq] query positions, or null (query i at position i)
+  const int* key_valid;      // [b][s] 1 = visible key
+  const float* cos;          // [max_len][64] or null (no rotary)
+  const float* sin;
+  int window;                // -1 global; else |q - k| <= window
+  __nv_bfloat16* out;        // [b*nq][ld_out]
+  int ld_out;
+};
+
+struct QuantParams {
+  int rows;
+  int k;
+  const __nv_bfloat16* src;  // [rows][k]
+  uint8_t* q;                // e4m3 [rows][k]  (fp8) or e2m1 [rows][k/2] (nvfp4)
+  float* scale;              // per-row fp32 scale (fp8) / outer (nvfp4)
+  uint8_t* sf;               // nvfp4 block scales in the MMA's tiled layout
+  int sf_cols;               // nvfp4: padded scale columns per row group
+};
+
+struct TailParams {
+  int k;                     // options per question
+  int d;
+  int act_hidden;
+  const __nv_bfloat16* z;    // gelu(scorer.fc1) rows [b*k][d]
+  const __nv_bfloat16* fc2_w;  // [d]
+  const __nv_bfloat16* fc2_b;  // [1]
+  const int* marker_mask;    // [b][k]
+  const float* h_sel;        // [b*(1+k)][d]; row 0 of each question is CLS
+  const __nv_bfloat16* a1_w;   // [act_hidden][d+4]
+  const __nv_bfloat16* a1_b;
+  const __nv_bfloat16* a2_w;   // [2][act_hidden]
+  const __nv_bfloat16* a2_b;
+  float* logits;             // [b][k]
+  float* act;                // [b][2]
+};
+
+}  // namespace laya

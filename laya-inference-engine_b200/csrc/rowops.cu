@@ -1,0 +1,340 @@
+// Row-wise kernels of the Laya forward: LayerNorm (with the embedding
+// gather, the type-embedding add and an optional second LayerNorm fused on the
+// same row), per-row FP8 activation quantisation, the head's row gather and
+// the decision tail (scorer logits, masked softmax, entropy, top-2, act_head).
+//
+// Reference: add_norm and the embedding LN (src/laya_blackwell/model.py:15-19,84,
+// 90,97,102-104,59,68), _quantize_rows (quantization.py:20-29), the select
+// gather (model.py:64-66,106) and the tail (model.py:113-123).
+//
+// One warp owns one row of d = 128*NV fp32 values kept in registers
+// (float4 per lane per chunk); reductions are warp shuffles.  LayerNorm uses
+// the two-pass mean / centred variance in fp32.
+#include "common.cuh"
+#include "params.h"
+#include "launch.h"
+
+namespace laya {
+
+namespace {
+
+template <int NV>
+DEVI void row_layernorm(float4 (&x)[NV], int d, float eps, const float* w, const float* b, int lane) {
+  float s = 0.f;
+#pragma unroll
+  for (int i = 0; i < NV; ++i) s += (x[i].x + x[i].y) + (x[i].z + x[i].w);
+  const float mean = warp_sum(s) / (float)d;
+  float v = 0.f;
+#pragma unroll
+  for (int i = 0; i < NV; ++i) {
+    const float a = x[i].x - mean, bb = x[i].y - mean, c = x[i].z - mean, e = x[i].w - mean;
+    v += (a * a + bb * bb) + (c * c + e * e);
+  }
+  const float var = warp_sum(v) / (float)d;
+  const float rstd = rsqrtf(var + eps);
+#pragma unroll
+  for (int i = 0; i < NV; ++i) {
+    const int col = (lane + 32 * i) * 4;
+    const float4 ww = *reinterpret_cast<const float4*>(w + col);
+    float4 bb = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (b) bb = *reinterpret_cast<const float4*>(b + col);
+    x[i].x = (x[i].x - mean) * rstd * ww.x + bb.x;
+    x[i].y = (x[i].y - mean) * rstd * ww.y + bb.y;
+    x[i].z = (x[i].z - mean) * rstd * ww.z + bb.z;
+    x[i].w = (x[i].w - mean) * rstd * ww.w + bb.w;
+  }
+}
+
+}  // namespace
+
+template <int NV>
+__global__ void __launch_bounds__(256) norm_kernel(const NormParams p) {
+  griddep_launch_dependents();
+  griddep_wait();
+  const int lane = threadIdx.x & 31;
+  const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (row >= p.rows) return;
+  const float* src;
+  if (p.tok_ids)
+    src = p.src + (size_t)p.tok_ids[row] * p.ld_src;
+  else
+    src = p.src + (size_t)(p.row_map ? p.row_map[row] : row) * p.ld_src;
+  float4 x[NV];
+#pragma unroll
+  for (int i = 0; i < NV; ++i) x[i] = reinterpret_cast<const float4*>(src)[lane + 32 * i];
+  row_layernorm<NV>(x, p.d, p.eps, p.w, p.b, lane);
+  if (p.add_table) {
+    const float* a = p.add_table + (size_t)p.add_idx[row / p.add_div] * p.d;
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+      const float4 t = reinterpret_cast<const float4*>(a)[lane + 32 * i];
+      x[i].x += t.x;
+      x[i].y += t.y;
+      x[i].z += t.z;
+      x[i].w += t.w;
+    }
+  }
+  if (p.out_f32) {
+    float4* dst = reinterpret_cast<float4*>(p.out_f32 + (size_t)row * p.ld_out_f32);
+#pragma unroll
+    for (int i = 0; i < NV; ++i) dst[lane + 32 * i] = x[i];
+  }
+  if (p.second_w) row_layernorm<NV>(x, p.d, p.eps, p.second_w, p.second_b, lane);
+  if (!p.out_bf16 && !p.out_fp8) return;
+  // bf16 of the row (also the FP8 quantiser's input, as in the reference where
+  // _quantize_rows reads the bf16 normed activations).
+  float amax = 0.f;
+#pragma unroll
+  for (int i = 0; i < NV; ++i) {
+    x[i].x = bf16_round(x[i].x);
+    x[i].y = bf16_round(x[i].y);
+    x[i].z = bf16_round(x[i].z);
+    x[i].w = bf16_round(x[i].w);
+    amax = fmaxf(amax, fmaxf(fmaxf(fabsf(x[i].x), fabsf(x[i].y)), fmaxf(fabsf(x[i].z), fabsf(x[i].w))));
+  }
+  if (p.out_bf16) {
+    __nv_bfloat16* dst = p.out_bf16 + (size_t)row * p.d;
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+      __nv_bfloat162 a = __floats2bfloat162_rn(x[i].x, x[i].y);
+      __nv_bfloat162 c = __floats2bfloat162_rn(x[i].z, x[i].w);
+      uint2 u;
+      u.x = *reinterpret_cast<uint32_t*>(&a);
+      u.y = *reinterpret_cast<uint32_t*>(&c);
+      *reinterpret_cast<uint2*>(dst + (lane + 32 * i) * 4) = u;
+    }
+  }
+  if (p.out_fp8) {
+    amax = warp_max(amax);
+    const float scale = fmaxf(amax / 448.0f, 1e-12f);
+    uint8_t* dst = p.out_fp8 + (size_t)row * p.d;
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+      const float a = fminf(fmaxf(x[i].x / scale, -448.f), 448.f);
+      const float bq = fminf(fmaxf(x[i].y / scale, -448.f), 448.f);
+      const float c = fminf(fmaxf(x[i].z / scale, -448.f), 448.f);
+      const float e = fminf(fmaxf(x[i].w / scale, -448.f), 448.f);
+      const uint32_t lo = f32x2_to_e4m3x2(a, bq), hi = f32x2_to_e4m3x2(c, e);
+      *reinterpret_cast<uint32_t*>(dst + (lane + 32 * i) * 4) = lo | (hi << 16);
+    }
+    if (lane == 0) p.out_fp8_scale[row] = scale;
+  }
+}
+
+// Per-row e4m3 quantisation of a bf16 matrix (quantization.py:20-29).
+__global__ void __launch_bounds__(256) quant_fp8_kernel(const QuantParams p) {
+  griddep_launch_dependents();
+  griddep_wait();
+  const int lane = threadIdx.x & 31;
+  const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (row >= p.rows) return;
+  const __nv_bfloat16* src = p.src + (size_t)row * p.k;
+  float amax = 0.f;
+  for (int c = lane * 8; c < p.k; c += 256) {
+    const uint4 u = *reinterpret_cast<const uint4*>(src + c);
+    const __nv_bfloat16* e = reinterpret_cast<const __nv_bfloat16*>(&u);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) amax = fmaxf(amax, fabsf(__bfloat162float(e[j])));
+  }
+  amax = warp_max(amax);
+  const float scale = fmaxf(amax / 448.0f, 1e-12f);
+  uint8_t* dst = p.q + (size_t)row * p.k;
+  for (int c = lane * 8; c < p.k; c += 256) {
+    const uint4 u = *reinterpret_cast<const uint4*>(src + c);
+    const __nv_bfloat16* e = reinterpret_cast<const __nv_bfloat16*>(&u);
+    uint32_t w[2];
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+      float v[4];
+#pragma unroll
+      for (int t = 0; t < 4; ++t) v[t] = fminf(fmaxf(__bfloat162float(e[4 * j + t]) / scale, -448.f), 448.f);
+      w[j] = (uint32_t)f32x2_to_e4m3x2(v[0], v[1]) | ((uint32_t)f32x2_to_e4m3x2(v[2], v[3]) << 16);
+    }
+    *reinterpret_cast<uint2*>(dst + c) = make_uint2(w[0], w[1]);
+  }
+  if (lane == 0) p.scale[row] = scale;
+}
+
+// dst[r] = src[map[r]] for fp32 rows of width d (multiple of 4).
+__global__ void __launch_bounds__(256) gather_rows_kernel(float* dst, const float* src, const int* map, int rows,
+                                                           int d) {
+  griddep_launch_dependents();
+  griddep_wait();
+  const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (row >= rows) return;
+  const float4* s = reinterpret_cast<const float4*>(src + (size_t)map[row] * d);
+  float4* o = reinterpret_cast<float4*>(dst + (size_t)row * d);
+  for (int c = lane; c < d / 4; c += 32) o[c] = s[c];
+}
+
+// One CTA per question: logits, softmax features and act_head (model.py:113-122).
+__global__ void __launch_bounds__(256) tail_kernel(const TailParams p) {
+  extern __shared__ float tsm[];
+  float* s_logit = tsm;                       // [k]
+  float* s_x = tsm + 256;                     // [d + 4] (bf16-rounded act_head input)
+  float* s_a1 = s_x + p.d + 8;                // [act_hidden]
+  griddep_launch_dependents();
+  griddep_wait();
+  const int q = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nw = blockDim.x >> 5;
+  // scorer[3]: logit_j = bf16(z_j . w + b), masked to -1e4
+  for (int j = warp; j < p.k; j += nw) {
+    const __nv_bfloat16* z = p.z + ((size_t)q * p.k + j) * p.d;
+    float acc = 0.f;
+    for (int c = lane; c < p.d; c += 32) acc += __bfloat162float(z[c]) * __bfloat162float(p.fc2_w[c]);
+    acc = warp_sum(acc);
+    if (lane == 0) {
+      const float l = bf16_round(acc + __bfloat162float(p.fc2_b[0]));
+      s_logit[j] = p.marker_mask[q * p.k + j] ? l : -1e4f;
+    }
+  }
+  // CLS row of the selected hidden states
+  const float* cls = p.h_sel + (size_t)q * (1 + p.k) * p.d;
+  for (int c = tid; c < p.d; c += blockDim.x) s_x[c] = bf16_round(cls[c]);
+  __syncthreads();
+  if (tid == 0) {
+    float mx = -INFINITY;
+    int count = 0;
+    for (int j = 0; j < p.k; ++j) {
+      mx = fmaxf(mx, s_logit[j]);
+      count += p.marker_mask[q * p.k + j] != 0;
+    }
+    float sum = 0.f;
+    for (int j = 0; j < p.k; ++j) sum += expf(s_logit[j] - mx);
+    float ent = 0.f, t1 = -1.f, t2 = -1.f;
+    for (int j = 0; j < p.k; ++j) {
+      const float pj = expf(s_logit[j] - mx) / sum;
+      ent += pj * logf(fmaxf(pj, 1e-9f));
+      if (pj > t1) {
+        t2 = t1;
+        t1 = pj;
+      } else if (pj > t2) {
+        t2 = pj;
+      }
+      p.logits[q * p.k + j] = s_logit[j];
+    }
+    const float cnt = (float)(count < 2 ? 2 : count);
+    ent = -ent / logf(cnt);
+    s_x[p.d + 0] = bf16_round(t1);
+    s_x[p.d + 1] = bf16_round(t1 - t2);
+    s_x[p.d + 2] = bf16_round(ent);
+    s_x[p.d + 3] = bf16_round(cnt / 255.0f);
+  }
+  __syncthreads();
+  // act_head[0..1]: a1 = bf16(gelu(bf16(W1 x + b1)))
+  const int din = p.d + 4;
+  for (int u = warp; u < p.act_hidden; u += nw) {
+    const __nv_bfloat16* wr = p.a1_w + (size_t)u * din;
+    float acc = 0.f;
+    for (int c = lane; c < din; c += 32) acc += __bfloat162float(wr[c]) * s_x[c];
+    acc = warp_sum(acc);
+    if (lane == 0) s_a1[u] = bf16_round(gelu_erf(bf16_round(acc + __bfloat162float(p.a1_b[u]))));
+  }
+  __syncthreads();
+  // act_head[2]: act = bf16(W2 a1 + b2)
+  if (warp < 2) {
+    const __nv_bfloat16* wr = p.a2_w + (size_t)warp * p.act_hidden;
+    float acc = 0.f;
+    for (int c = lane; c < p.act_hidden; c += 32) acc += __bfloat162float(wr[c]) * s_a1[c];
+    acc = warp_sum(acc);
+    if (lane == 0) p.act[q * 2 + warp] = bf16_round(acc + __bfloat162float(p.a2_b[warp]));
+  }
+}
+
+// Per-output-row e4m3 weight quantisation (quantization.py:62-73), bf16 in.
+__global__ void __launch_bounds__(256) pack_fp8_rows_kernel(const __nv_bfloat16* w, uint8_t* q, float* scale, int rows,
+                                                            int k) {
+  QuantParams p;
+  p.rows = rows;
+  p.k = k;
+  p.src = w;
+  p.q = q;
+  p.scale = scale;
+  const int lane = threadIdx.x & 31;
+  const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (row >= rows) return;
+  const __nv_bfloat16* src = p.src + (size_t)row * k;
+  float amax = 0.f;
+  for (int c = lane; c < k; c += 32) amax = fmaxf(amax, fabsf(__bfloat162float(src[c])));
+  amax = warp_max(amax);
+  const float s = fmaxf(amax / 448.0f, 1e-12f);
+  for (int c = lane * 2; c < k; c += 64) {
+    const float a = fminf(fmaxf(__bfloat162float(src[c]) / s, -448.f), 448.f);
+    const float b = fminf(fmaxf(__bfloat162float(src[c + 1]) / s, -448.f), 448.f);
+    *reinterpret_cast<uint16_t*>(q + (size_t)row * k + c) = f32x2_to_e4m3x2(a, b);
+  }
+  if (lane == 0) scale[row] = s;
+}
+
+// ------------------------------------------------------------------ launchers
+namespace {
+cudaError_t launch_rows(const void* kern, void** args, int rows, size_t smem, cudaStream_t stream, bool pdl) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((rows + 7) / 8, 1, 1);
+  cfg.blockDim = dim3(256, 1, 1);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr;
+  attr.id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr.val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = &attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  return cudaLaunchKernelExC(&cfg, kern, args);
+}
+}  // namespace
+
+cudaError_t launch_norm(const NormParams& p, cudaStream_t stream, bool pdl) {
+  if (p.d % 128 || p.d > 1024 || p.d < 128) return cudaErrorInvalidValue;
+  NormParams q = p;
+  void* args[] = {&q};
+  const void* kern = nullptr;
+  switch (p.d / 128) {
+    case 1: kern = (const void*)norm_kernel<1>; break;
+    case 2: kern = (const void*)norm_kernel<2>; break;
+    case 3: kern = (const void*)norm_kernel<3>; break;
+    case 4: kern = (const void*)norm_kernel<4>; break;
+    case 5: kern = (const void*)norm_kernel<5>; break;
+    case 6: kern = (const void*)norm_kernel<6>; break;
+    case 7: kern = (const void*)norm_kernel<7>; break;
+    case 8: kern = (const void*)norm_kernel<8>; break;
+  }
+  return launch_rows(kern, args, p.rows, 0, stream, pdl);
+}
+
+cudaError_t launch_quant_fp8(const QuantParams& p, cudaStream_t stream, bool pdl) {
+  if (p.k % 8) return cudaErrorInvalidValue;
+  QuantParams q = p;
+  void* args[] = {&q};
+  return launch_rows((const void*)quant_fp8_kernel, args, p.rows, 0, stream, pdl);
+}
+
+cudaError_t launch_gather_rows(float* dst, const float* src, const int* map, int rows, int d, cudaStream_t stream,
+                               bool pdl) {
+  void* args[] = {&dst, &src, &map, &rows, &d};
+  return launch_rows((const void*)gather_rows_kernel, args, rows, 0, stream, pdl);
+}
+
+cudaError_t launch_tail(const TailParams& p, int batch, cudaStream_t stream, bool pdl) {
+  if (p.k > 256) return cudaErrorInvalidValue;
+  TailParams q = p;
+  void* args[] = {&q};
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(batch, 1, 1);
+  cfg.blockDim = dim3(256, 1, 1);
+  cfg.dynamicSmemBytes = (256 + p.d + 8 + p.act_hidden) * sizeof(float);
+  cfg.stream = stream;
+  cudaLaunchAttribute attr;
+  attr.id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr.val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = &attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  return cudaLaunchKernelExC(&cfg, (const void*)tail_kernel, args);
+}
+
+cudaError_t launch_pack_fp8_rows(const __nv_bfloat16* w, uint8_t* q, float* scale, int rows, int k,
+                                 cudaStream_t stream) {
+  pack_fp8_rows_kernel<<<(rows + 7) / 8, 256, 0, stream>>>(w, q, scale, rows, k);
+  return cudaGetLastError();
+}
+
+}  // namespace laya

@@ -1,0 +1,114 @@
+"""Kernel-level parity on a one-layer network: every stage of the CUDA forward
+against the CPU oracle, each stage fed with the GPU's own previous stage so a
+mismatch points at one kernel.  Calls the library through the C ABI."""
+import numpy as np
+import pytest
+import torch
+
+from laya_b200.config import LayaConfig
+from laya_b200.weights import seeded_weights, as_float32, bf16_bits_to_f32
+from laya_b200.workload import synthetic_items, pack
+from oracle import laya_oracle as O
+
+pytestmark = pytest.mark.gpu
+
+MICRO = LayaConfig(layers=1, hidden=256, heads=4, intermediate=384, vocab=1000, pad_token_id=999, max_len=512,
+                   head_layers=0, head_heads=4, head_ff=512, act_hidden=64)
+MICRO_LOCAL = LayaConfig(layers=2, hidden=256, heads=4, intermediate=384, vocab=1000, pad_token_id=999,
+                         max_len=512, head_layers=1, head_heads=4, head_ff=512, act_hidden=64)
+
+
+def bf16_of(u16):
+    return torch.from_numpy(bf16_bits_to_f32(u16))
+
+
+def frac_mismatch(a, b, atol):
+    return float((np.abs(a - b) > atol).mean())
+
+
+@pytest.fixture(scope="module")
+def micro():
+    from laya_b200.engine import NativeForward
+    w = seeded_weights(MICRO, seed=3)
+    nf = NativeForward(0, MICRO, w, "bf16", max_batch=4, max_options=8)
+    yield nf, w
+    nf.close()
+
+
+def test_stages_match_oracle(micro):
+    nf, w = micro
+    cfg = MICRO
+    b, s, k = 2, 192, 4
+    items = synthetic_items([192, 100], ["choice", "noul"], seed=11, vocab=cfg.vocab)
+    inp = pack(items, b, s, k, cfg.pad_token_id)
+    slot = nf.capture(b, s, k, False)
+    logits, act = nf.run(slot, inp)
+    T, d, I = b * s, cfg.hidden, cfg.intermediate
+    wf = {kk: torch.from_numpy(v) for kk, v in as_float32(w).items()}
+    qkv = bf16_of(nf.read_buffer("qkv", (T, 3 * d), np.uint16).view(np.uint16))
+    attn = bf16_of(nf.read_buffer("attn", (T, d), np.uint16))
+    g = bf16_of(nf.read_buffer("g", (T, I), np.uint16))
+    h = torch.from_numpy(nf.read_buffer("h", (T, d), np.float32))
+    report = {}
+    ids = torch.from_numpy(inp["input_ids"]).reshape(-1)
+    h0 = O.layer_norm(wf["embed.tok"][ids], wf["embed.norm.w"], None, cfg.norm_eps)
+    n0 = O.bf16(h0)
+    qkv_ref = O.linear(n0, wf["enc.0.wqkv"])
+    report["qkv"] = (float((qkv - qkv_ref).abs().max()), frac_mismatch(qkv.numpy(), qkv_ref.numpy(), 1e-6))
+    # attention from the GPU's own qkv (global layer 0, key padding)
+    gcos, gsin = O.rope_tables(cfg.rope_theta_global, cfg.max_len, 64)
+    q5 = qkv.view(b, s, 3, cfg.heads, 64)
+    q = O.rope(q5[:, :, 0], gcos, gsin).permute(0, 2, 1, 3)
+    kk_ = O.rope(q5[:, :, 1], gcos, gsin).permute(0, 2, 1, 3)
+    v = q5[:, :, 2].permute(0, 2, 1, 3)
+    vis = torch.from_numpy(inp["attention_mask"]).bool()[:, None, None, :]
+    attn_ref = O.attention(q, kk_, v, vis).transpose(1, 2).reshape(T, d)
+    report["attn"] = (float((attn - attn_ref).abs().max()), frac_mismatch(attn.numpy(), attn_ref.numpy(), 1e-6))
+    h1 = h0 + O.linear(attn, wf["enc.0.wo"])
+    n1 = O.bf16(O.layer_norm(h1, wf["enc.0.mlp_norm.w"], None, cfg.norm_eps))
+    y = O.linear(n1, wf["enc.0.wi"])
+    a_, gate = y.chunk(2, dim=-1)
+    g_ref = O.bf16(O.bf16(O.gelu(a_)) * gate)
+    report["geglu"] = (float((g - g_ref).abs().max()), frac_mismatch(g.numpy(), g_ref.numpy(), 1e-6))
+    h2 = h1 + O.linear(g, wf["enc.0.wo2"])
+    qt = torch.from_numpy(inp["qtype"])
+    hf = O.layer_norm(h2, wf["final_norm.w"], None, cfg.norm_eps).view(b, s, d) + wf["type_emb"][qt][:, None, :]
+    report["final_h"] = (float((h.view(b, s, d) - hf).abs().max()), 0.0)
+    # whole forward against the oracle
+    orc = O.Oracle(w, cfg)
+    ol, oa = orc.forward(**inp)
+    mm = inp["marker_mask"]
+    report["logits"] = (float(np.abs(logits[mm] - ol[mm]).max()), 0.0)
+    report["act"] = (float(np.abs(act - oa).max()), 0.0)
+    print("stage max-abs / mismatch-fraction:", report)
+    assert report["qkv"][0] < 2e-2 and report["qkv"][1] < 0.02, report
+    assert report["attn"][0] < 2e-2 and report["attn"][1] < 0.05, report
+    assert report["geglu"][0] < 2e-2 and report["geglu"][1] < 0.05, report
+    assert report["final_h"][0] < 2e-2, report
+    assert report["logits"][0] < 2e-2 and report["act"][0] < 2e-2, report
+    assert np.array_equal(logits[~mm], np.full((~mm).sum(), -1e4, np.float32))
+
+
+def test_local_window_and_head_select():
+    from laya_b200.engine import NativeForward
+    cfg = MICRO_LOCAL
+    w = seeded_weights(cfg, seed=5)
+    nf = NativeForward(0, cfg, w, "bf16", max_batch=4, max_options=8)
+    try:
+        orc = O.Oracle(w, cfg)
+        # 300 valid tokens in a 384 bucket: padded queries beyond the radius see no key.
+        for lengths, s in (([300, 40, 7], 384), ([64], 64), ([129, 130], 160)):
+            b = 1 << (len(lengths) - 1).bit_length()
+            kinds = ["choice", "score", "noul"][: len(lengths)]
+            items = synthetic_items(lengths, kinds, seed=len(lengths) + s, vocab=cfg.vocab)
+            inp = pack(items, b, s, 4, cfg.pad_token_id)
+            slot = nf.capture(b, s, 4, False)
+            logits, act = nf.run(slot, inp)
+            ol, oa = orc.forward(**inp)
+            mm = inp["marker_mask"]
+            err = float(np.abs(logits[mm] - ol[mm]).max())
+            aerr = float(np.abs(act - oa).max())
+            assert err < 2e-2 and aerr < 2e-2, (lengths, s, err, aerr)
+            assert np.isfinite(logits).all() and np.isfinite(act).all()
+    finally:
+        nf.close()

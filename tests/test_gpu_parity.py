@@ -1,0 +1,131 @@
+"""Full-forward parity of the CUDA path (through the C ABI) against the CPU
+oracle and against the reference's own outputs stored in tests/golden.
+
+Tolerances (max-abs on valid logits and on act): bf16 2e-2, fp8 6e-2,
+nvfp4 1.5e-1, compared with the oracle of the same precision.  Decisions
+(argmax over real options) must agree wherever the reference's top-2 logit
+margin exceeds the tolerance; the overall agreement rate is printed.
+"""
+import functools
+from pathlib import Path
+
+import numpy as np
+import pytest
+
+from laya_b200.config import LAYA, TINY
+from laya_b200.weights import seeded_weights
+from laya_b200.workload import synthetic_items, pack, mixed_kinds
+from oracle import laya_oracle as O
+
+pytestmark = pytest.mark.gpu
+
+GOLDEN = Path(__file__).parent / "golden"
+CONFIGS = {"laya": LAYA, "tiny": TINY}
+TOL = {"bf16": 2e-2, "fp8": 6e-2, "nvfp4": 1.5e-1}
+KEYS = ("input_ids", "attention_mask", "marker_pos", "marker_mask", "qtype")
+
+
+@functools.lru_cache(maxsize=1)
+def weights_for(name):
+    return seeded_weights(CONFIGS[name], seed=0)
+
+
+_ENGINES = {}
+
+
+def engine_for(name, precision):
+    from laya_b200.engine import NativeForward
+    key = (name, precision)
+    if key not in _ENGINES:
+        for other in list(_ENGINES):
+            _ENGINES.pop(other).close()
+        _ENGINES[key] = NativeForward(0, CONFIGS[name], weights_for(name), precision, max_batch=16,
+                                      max_options=8)
+    return _ENGINES[key]
+
+
+@functools.lru_cache(maxsize=2)
+def oracle_for(name, precision):
+    return O.Oracle(weights_for(name), CONFIGS[name], precision)
+
+
+def teardown_module(_):
+    for k in list(_ENGINES):
+        _ENGINES.pop(k).close()
+
+
+def compare(logits, act, ref_logits, ref_act, mm, tol, label):
+    mm = mm.astype(bool)
+    err = float(np.abs(logits[mm] - ref_logits[mm]).max())
+    aerr = float(np.abs(act - ref_act).max())
+    margins = O.top2_margin(ref_logits, mm)
+    agree = O.decision_agreement(ref_logits, logits, mm)
+    decided = margins > tol
+    agree_decided = O.decision_agreement(ref_logits[decided], logits[decided], mm[decided]) if decided.any() else 1.0
+    print(f"{label}: logit max-abs {err:.3e}, act max-abs {aerr:.3e}, agreement {agree:.3f}, "
+          f"agreement where margin>{tol} {agree_decided:.3f}")
+    assert err <= tol and aerr <= tol, (label, err, aerr)
+    assert agree_decided == 1.0, label
+    assert np.array_equal(logits[~mm], np.full((~mm).sum(), -1e4, np.float32))
+
+
+@pytest.mark.parametrize("path", sorted(GOLDEN.glob("*.npz")), ids=lambda p: p.stem)
+def test_bf16_matches_reference_golden(path):
+    z = np.load(path)
+    name = str(z["config"])
+    inputs = {k: z[k] for k in KEYS}
+    b, s = inputs["input_ids"].shape
+    k = inputs["marker_pos"].shape[1]
+    nf = engine_for(name, "bf16")
+    slot = nf.capture(b, s, k, bool(z["unmasked"]))
+    logits, act = nf.run(slot, inputs)
+    n = int(z["n_items"])
+    compare(logits[:n], act[:n], z["ref_logits"][:n], z["ref_act"][:n], inputs["marker_mask"][:n], TOL["bf16"],
+            f"{path.stem} vs reference")
+    ol, oa = oracle_for(name, "bf16").forward(**inputs)
+    compare(logits[:n], act[:n], ol[:n], oa[:n], inputs["marker_mask"][:n], TOL["bf16"], f"{path.stem} vs oracle")
+
+
+def test_replay_is_deterministic_and_slots_are_reusable():
+    nf = engine_for("tiny", "bf16")
+    items = synthetic_items([90, 64], ["choice", "noul"], seed=21, vocab=TINY.vocab)
+    inp = pack(items, 2, 96, 4, TINY.pad_token_id)
+    slot = nf.capture(2, 96, 4, False)
+    a = nf.run(slot, inp)
+    other = pack(synthetic_items([33], ["score"], seed=22, vocab=TINY.vocab), 2, 96, 4, TINY.pad_token_id)
+    nf.run(slot, other)
+    b = nf.run(slot, inp)
+    assert np.array_equal(a[0], b[0]) and np.array_equal(a[1], b[1])
+
+
+def test_invalid_inputs_are_rejected_on_the_host():
+    nf = engine_for("tiny", "bf16")
+    inp = pack(synthetic_items([20], ["noul"], seed=1, vocab=TINY.vocab), 1, 64, 2, TINY.pad_token_id)
+    slot = nf.capture(1, 64, 2, False)
+    bad = dict(inp, input_ids=inp["input_ids"].copy())
+    bad["input_ids"][0, 3] = TINY.vocab
+    with pytest.raises(RuntimeError, match="input_ids"):
+        nf.run(slot, bad)
+    bad = dict(inp, marker_pos=inp["marker_pos"].copy())
+    bad["marker_pos"][0, 1] = 64
+    with pytest.raises(RuntimeError, match="marker_pos"):
+        nf.run(slot, bad)
+    nf.run(slot, inp)  # the engine stays usable
+
+
+@pytest.mark.parametrize("name,lengths,s,k", [
+    ("laya", [96] * 10 + [70, 41, 96, 88, 17, 64], 96, 4),    # C2 shape: 16 questions x 96
+])
+def test_fp8_matches_fp8_oracle(name, lengths, s, k):
+    nf = engine_for(name, "fp8")
+    kinds = mixed_kinds(len(lengths), seed=3)
+    items = synthetic_items(lengths, kinds, seed=30, vocab=CONFIGS[name].vocab)
+    b = len(lengths)
+    inp = pack(items, b, s, k, CONFIGS[name].pad_token_id)
+    slot = nf.capture(b, s, k, False)
+    logits, act = nf.run(slot, inp)
+    ol, oa = oracle_for(name, "fp8").forward(**inp)
+    compare(logits, act, ol, oa, inp["marker_mask"], TOL["fp8"], "fp8 C2 vs fp8 oracle")
+    bl, _ = oracle_for(name, "bf16").forward(**inp)
+    agree = O.decision_agreement(bl, logits, inp["marker_mask"])
+    print(f"fp8 decision agreement with the bf16 oracle: {agree:.3f}")
