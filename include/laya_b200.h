@@ -77,10 +77,15 @@ LAYA_B200_API int laya_b200_run(laya_b200_engine* e, int slot, const int64_t* in
                   const int64_t* marker_pos, const uint8_t* marker_mask, const int64_t* qtype, float* logits,
                   float* act);
 
-/* Benchmark helper: replay the kernels-only graph `iterations` times on the
- * inputs already resident on the device (from the last run) and return the
- * mean device time per forward in milliseconds (CUDA events). */
-LAYA_B200_API int laya_b200_replay_device(laya_b200_engine* e, int slot, int iterations, float* ms_per_forward);
+/* Measurement helper: replay the kernels-only graph `iterations` times back
+ * to back on the inputs already resident on the device (from the last run)
+ * and write each replay's device time in milliseconds (CUDA events on the
+ * engine's stream) to ms_each[iterations].  kernel_mask selects the kernel
+ * families in the replayed graph: 1 projections (GEMM), 2 attention, 4 row
+ * kernels (norms, quantisation, gather, tail); 7 is the whole forward.
+ * Partial masks compute garbage and exist only to time one family. */
+LAYA_B200_API int laya_b200_replay_device(laya_b200_engine* e, int slot, int iterations, int kernel_mask,
+                                          float* ms_each);
 
 /* Number of kernels one forward of the slot launches. */
 LAYA_B200_API int laya_b200_kernel_count(laya_b200_engine* e, int slot, int* count);

@@ -105,10 +105,38 @@ struct Shape {
   int b, s, k, unmasked;
 };
 
+// Compact per-shape layout of the int32 input words and fp32 output words, so
+// each step copies only what the shape needs.
+struct IoLayout {
+  size_t ids, valid, qtype, mmask, selsrc, selpos, score, words;
+  size_t logits, act, out_words;
+};
+
+IoLayout io_layout(const Shape& sh) {
+  IoLayout L{};
+  const size_t b = sh.b, T = (size_t)sh.b * sh.s, R = (size_t)sh.b * (1 + sh.k), BK = (size_t)sh.b * sh.k;
+  size_t o = 0;
+  L.ids = o; o += T;
+  L.valid = o; o += T;
+  L.qtype = o; o += b;
+  L.mmask = o; o += BK;
+  L.selsrc = o; o += R;
+  L.selpos = o; o += R;
+  L.score = o; o += BK;
+  L.words = o;
+  L.logits = 0;
+  L.act = BK;
+  L.out_words = BK + 2 * b;
+  return L;
+}
+
+// Kernel categories for partial replays (timing of one kernel family).
+enum : int { kCatGemm = 1, kCatAttention = 2, kCatRows = 4, kCatAll = 7 };
+
 struct Slot {
   Shape sh;
   cudaGraphExec_t io_exec = nullptr;   // H2D + kernels + D2H
-  cudaGraphExec_t dev_exec = nullptr;  // kernels only
+  cudaGraphExec_t dev_exec[8] = {};    // kernels only, by category mask
   int kernels = 0;
   bool live = false;
 };
@@ -159,9 +187,7 @@ struct laya_b200_engine {
   std::vector<Slot> slots;
   int launches = 0;  // counter while enqueuing
 
-  // input section offsets (words), computed from the capacity
-  size_t off_ids = 0, off_valid = 0, off_qtype = 0, off_mmask = 0, off_selsrc = 0, off_selpos = 0,
-         off_score = 0;
+  std::vector<cudaEvent_t> timing_events;
 };
 
 namespace {
@@ -252,8 +278,10 @@ void rope_tables(float theta, int max_len, std::vector<float>& cs, std::vector<f
 struct Fwd {
   laya_b200_engine* e;
   cudaStream_t st;
+  int mask = kCatAll;  // enqueue only kernels of these categories
   bool first = true;
 
+  bool on(int cat) const { return (mask & cat) != 0; }
   bool pdl() {
     const bool r = !first;
     first = false;
@@ -267,6 +295,7 @@ struct Fwd {
 
   void gemm(const Proj& w, const void* x, const float* x_scale, int M, int epi, __nv_bfloat16* out, int ldo,
             float* resid, int ldr) {
+    if (!on(kCatGemm)) return;
     const int bn = gemm_token_tile(M);
     const int esize = w.kind == kKindBf16 ? 2 : 1;
     CUtensorMap xmap = make_map(x, M, w.K, esize, bn);
@@ -290,12 +319,14 @@ struct Fwd {
   }
 
   void norm(NormParams p) {
+    if (!on(kCatRows)) return;
     p.eps = e->cfg.norm_eps;
     p.d = e->cfg.hidden;
     count(launch_norm(p, st, pdl()), "norm launch");
   }
 
   void attention(const AttnParams& p, int batch, int heads) {
+    if (!on(kCatAttention)) return;
     count(launch_attention(p, batch, heads, st, pdl()), "attention launch");
   }
 
@@ -305,14 +336,15 @@ struct Fwd {
     const int b = sh.b, s = sh.s, k = sh.k, d = c.hidden, I = c.intermediate, F = c.head_ff;
     const int T = b * s, R = b * (1 + k), BK = b * k;
     const bool fp8 = E.precision == LAYA_B200_FP8;
+    const IoLayout L = io_layout(sh);
     const int32_t* in = E.d_in;
-    const int* ids = in + E.off_ids;
-    const int* valid = in + E.off_valid;
-    const int* qtype = in + E.off_qtype;
-    const int* mmask = in + E.off_mmask;
-    const int* selsrc = in + E.off_selsrc;
-    const int* selpos = in + E.off_selpos;
-    const int* score_rows = in + E.off_score;
+    const int* ids = in + L.ids;
+    const int* valid = in + L.valid;
+    const int* qtype = in + L.qtype;
+    const int* mmask = in + L.mmask;
+    const int* selsrc = in + L.selsrc;
+    const int* selpos = in + L.selpos;
+    const int* score_rows = in + L.score;
 
     // enc.embeddings: gather + LayerNorm; layer 0 consumes bf16(h) (model.py:84,87-88)
     {
@@ -365,7 +397,7 @@ struct Fwd {
         a.ld_out = d;
         attention(a, b, c.heads);
       }
-      if (fp8) {
+      if (fp8 && on(kCatRows)) {
         QuantParams q{};
         q.rows = T;
         q.k = d;
@@ -390,7 +422,7 @@ struct Fwd {
         norm(p);
       }
       gemm(E.wi[i], fp8 ? (const void*)E.n8 : (const void*)E.n, E.n8s, T, kEpiGeglu, E.g, I, nullptr, 0);
-      if (fp8) {
+      if (fp8 && on(kCatRows)) {
         QuantParams q{};
         q.rows = T;
         q.k = I;
@@ -457,7 +489,7 @@ struct Fwd {
         a.q_pos = selpos;
         a.out = E.asel;
         attention(a, b, c.head_heads);
-        count(launch_gather_rows(E.hsel, E.h, selsrc, R, d, st, pdl()), "gather launch");
+        if (on(kCatRows)) count(launch_gather_rows(E.hsel, E.h, selsrc, R, d, st, pdl()), "gather launch");
         hrows = E.hsel;
         rows = R;
         arows = E.asel;
@@ -478,7 +510,7 @@ struct Fwd {
       gemm(E.lin1[j], nrows, nullptr, rows, kEpiRelu, frows, F, nullptr, 0);
       gemm(E.lin2[j], frows, nullptr, rows, kEpiResidual, nullptr, 0, hrows, d);
     }
-    if (c.head_layers == 0)
+    if (c.head_layers == 0 && on(kCatRows))
       count(launch_gather_rows(E.hsel, E.h, selsrc, R, d, st, pdl()), "gather launch");
     // scorer: LN -> bf16 -> Linear -> GELU (model.py:113-114)
     {
@@ -493,7 +525,7 @@ struct Fwd {
       norm(p);
     }
     gemm(E.sc_fc1, E.msc, nullptr, BK, kEpiGelu, E.zsc, d, nullptr, 0);
-    {
+    if (on(kCatRows)) {
       TailParams t{};
       t.k = k;
       t.d = d;
@@ -507,8 +539,8 @@ struct Fwd {
       t.a1_b = wptr<__nv_bfloat16>(e, "act.fc1.b");
       t.a2_w = wptr<__nv_bfloat16>(e, "act.fc2.w");
       t.a2_b = wptr<__nv_bfloat16>(e, "act.fc2.b");
-      t.logits = E.d_out;
-      t.act = E.d_out + (size_t)c.max_batch * c.max_options;
+      t.logits = E.d_out + L.logits;
+      t.act = E.d_out + L.act;
       count(launch_tail(t, b, st, pdl()), "tail launch");
     }
   }
@@ -535,8 +567,38 @@ Proj make_proj(laya_b200_engine* e, const std::string& wname, const std::string&
 
 void free_slot(Slot& s) {
   if (s.io_exec) cudaGraphExecDestroy(s.io_exec);
-  if (s.dev_exec) cudaGraphExecDestroy(s.dev_exec);
+  for (auto& g : s.dev_exec)
+    if (g) cudaGraphExecDestroy(g);
   s = Slot{};
+}
+
+// Capture one forward (kernels of the categories in `mask`) into a graph;
+// with_io adds the H2D copy of the shape's inputs and the D2H copy of its
+// outputs around the kernels.
+cudaGraphExec_t capture_graph(laya_b200_engine* e, const Shape& sh, int mask, bool with_io, int* kernels) {
+  const IoLayout L = io_layout(sh);
+  cudaGraph_t graph = nullptr;
+  ck(cudaStreamBeginCapture(e->stream, cudaStreamCaptureModeThreadLocal), "begin capture");
+  try {
+    if (with_io)
+      ck(cudaMemcpyAsync(e->d_in, e->h_in, L.words * 4, cudaMemcpyHostToDevice, e->stream), "H2D");
+    e->launches = 0;
+    Fwd f{e, e->stream, mask};
+    f.run(sh);
+    if (kernels) *kernels = e->launches;
+    if (with_io)
+      ck(cudaMemcpyAsync(e->h_out, e->d_out, L.out_words * 4, cudaMemcpyDeviceToHost, e->stream), "D2H");
+  } catch (...) {
+    cudaStreamEndCapture(e->stream, &graph);
+    if (graph) cudaGraphDestroy(graph);
+    throw;
+  }
+  ck(cudaStreamEndCapture(e->stream, &graph), "end capture");
+  cudaGraphExec_t exec = nullptr;
+  cudaError_t err = cudaGraphInstantiate(&exec, graph, 0);
+  cudaGraphDestroy(graph);
+  ck(err, "graph instantiate");
+  return exec;
 }
 
 int guard(laya_b200_engine* e, const std::function<void()>& fn) {
@@ -633,16 +695,10 @@ int laya_b200_create(int device, const laya_b200_config* cfg, laya_b200_engine**
     rope_tables(c.rope_theta_local, c.max_len, cs, sn);
     ck(cudaMemcpy(e->lcos, cs.data(), cs.size() * 4, cudaMemcpyHostToDevice), "rope upload");
     ck(cudaMemcpy(e->lsin, sn.data(), sn.size() * 4, cudaMemcpyHostToDevice), "rope upload");
-    // I/O staging: int32 words [ids T | valid T | qtype B | mmask BK | selsrc R | selpos R | score BK]
-    e->off_ids = 0;
-    e->off_valid = T;
-    e->off_qtype = 2 * T;
-    e->off_mmask = e->off_qtype + c.max_batch;
-    e->off_selsrc = e->off_mmask + BK;
-    e->off_selpos = e->off_selsrc + R;
-    e->off_score = e->off_selpos + R;
-    e->in_words = e->off_score + BK;
-    e->out_words = BK + (size_t)c.max_batch * 2;
+    // I/O staging capacity: the layout of the largest shape
+    const IoLayout cap = io_layout(Shape{c.max_batch, c.max_len, c.max_options, 0});
+    e->in_words = cap.words;
+    e->out_words = cap.out_words;
     ck(cudaMalloc(&e->d_in, e->in_words * 4), "input buffer");
     ck(cudaMemset(e->d_in, 0, e->in_words * 4), "input memset");
     ck(cudaMalloc(&e->d_out, e->out_words * 4), "output buffer");
@@ -766,29 +822,12 @@ int laya_b200_capture(laya_b200_engine* e, int batch, int seq, int options, int 
     if (options < 2 || options > c.max_options) fail("options %d outside [2, %d]", options, c.max_options);
     Slot s;
     s.sh = Shape{batch, seq, options, unmasked ? 1 : 0};
-    for (int variant = 0; variant < 2; ++variant) {
-      cudaGraph_t graph = nullptr;
-      ck(cudaStreamBeginCapture(e->stream, cudaStreamCaptureModeThreadLocal), "begin capture");
-      try {
-        if (variant == 0)
-          ck(cudaMemcpyAsync(e->d_in, e->h_in, e->in_words * 4, cudaMemcpyHostToDevice, e->stream), "H2D");
-        e->launches = 0;
-        Fwd f{e, e->stream};
-        f.run(s.sh);
-        s.kernels = e->launches;
-        if (variant == 0)
-          ck(cudaMemcpyAsync(e->h_out, e->d_out, e->out_words * 4, cudaMemcpyDeviceToHost, e->stream), "D2H");
-      } catch (...) {
-        cudaStreamEndCapture(e->stream, &graph);
-        if (graph) cudaGraphDestroy(graph);
-        throw;
-      }
-      ck(cudaStreamEndCapture(e->stream, &graph), "end capture");
-      cudaGraphExec_t exec = nullptr;
-      cudaError_t err = cudaGraphInstantiate(&exec, graph, 0);
-      cudaGraphDestroy(graph);
-      ck(err, "graph instantiate");
-      (variant == 0 ? s.io_exec : s.dev_exec) = exec;
+    try {
+      s.io_exec = capture_graph(e, s.sh, kCatAll, true, &s.kernels);
+      s.dev_exec[kCatAll] = capture_graph(e, s.sh, kCatAll, false, nullptr);
+    } catch (...) {
+      free_slot(s);
+      throw;
     }
     s.live = true;
     for (size_t i = 0; i < e->slots.size(); ++i)
@@ -820,26 +859,27 @@ int laya_b200_run(laya_b200_engine* e, int slot, const int64_t* input_ids, const
     const Slot& sl = e->slots[slot];
     const int b = sl.sh.b, s = sl.sh.s, k = sl.sh.k;
     const laya_b200_config& c = e->cfg;
+    const IoLayout L = io_layout(sl.sh);
     int32_t* w = e->h_in;
     // Pack and validate on the host; nothing out of range reaches a kernel.
     for (int i = 0; i < b * s; ++i) {
       const int64_t id = input_ids[i];
       if (id < 0 || id >= c.vocab) fail("input_ids[%d]=%lld outside [0, %d)", i, (long long)id, c.vocab);
-      w[e->off_ids + i] = (int32_t)id;
-      w[e->off_valid + i] = attention_mask[i] != 0;
+      w[L.ids + i] = (int32_t)id;
+      w[L.valid + i] = attention_mask[i] != 0;
     }
     for (int q = 0; q < b; ++q) {
       if (qtype[q] < 0 || qtype[q] >= c.num_qtypes) fail("qtype[%d]=%lld out of range", q, (long long)qtype[q]);
-      w[e->off_qtype + q] = (int32_t)qtype[q];
-      w[e->off_selsrc + q * (1 + k)] = q * s;
-      w[e->off_selpos + q * (1 + k)] = 0;
+      w[L.qtype + q] = (int32_t)qtype[q];
+      w[L.selsrc + q * (1 + k)] = q * s;
+      w[L.selpos + q * (1 + k)] = 0;
       for (int j = 0; j < k; ++j) {
         const int64_t pos = marker_pos[q * k + j];
         if (pos < 0 || pos >= s) fail("marker_pos[%d][%d]=%lld outside [0, %d)", q, j, (long long)pos, s);
-        w[e->off_mmask + q * k + j] = marker_mask[q * k + j] != 0;
-        w[e->off_selsrc + q * (1 + k) + 1 + j] = q * s + (int32_t)pos;
-        w[e->off_selpos + q * (1 + k) + 1 + j] = (int32_t)pos;
-        w[e->off_score + q * k + j] = q * (1 + k) + 1 + j;
+        w[L.mmask + q * k + j] = marker_mask[q * k + j] != 0;
+        w[L.selsrc + q * (1 + k) + 1 + j] = q * s + (int32_t)pos;
+        w[L.selpos + q * (1 + k) + 1 + j] = (int32_t)pos;
+        w[L.score + q * k + j] = q * (1 + k) + 1 + j;
       }
     }
     ck(cudaGraphLaunch(sl.io_exec, e->stream), "graph launch");
@@ -849,27 +889,34 @@ int laya_b200_run(laya_b200_engine* e, int slot, const int64_t* input_ids, const
       e->status_host[0] = 0;
       fail("a device-side wait timed out (status %u); the results of this call are invalid", st);
     }
-    memcpy(logits, e->h_out, sizeof(float) * b * k);
-    memcpy(act, e->h_out + (size_t)c.max_batch * c.max_options, sizeof(float) * b * 2);
+    memcpy(logits, e->h_out + L.logits, sizeof(float) * b * k);
+    memcpy(act, e->h_out + L.act, sizeof(float) * b * 2);
   });
 }
 
-int laya_b200_replay_device(laya_b200_engine* e, int slot, int iterations, float* ms) {
+int laya_b200_replay_device(laya_b200_engine* e, int slot, int iterations, int kernel_mask, float* ms_each) {
   return guard(e, [&] {
     if (slot < 0 || slot >= (int)e->slots.size() || !e->slots[slot].live) fail("no slot %d", slot);
-    if (iterations < 1 || !ms) fail("bad arguments");
-    const Slot& sl = e->slots[slot];
-    ck(cudaEventRecord(e->ev0, e->stream), "event");
-    for (int i = 0; i < iterations; ++i) ck(cudaGraphLaunch(sl.dev_exec, e->stream), "graph launch");
-    ck(cudaEventRecord(e->ev1, e->stream), "event");
-    ck(cudaEventSynchronize(e->ev1), "replay");
-    float t = 0.f;
-    ck(cudaEventElapsedTime(&t, e->ev0, e->ev1), "elapsed");
+    if (iterations < 1 || !ms_each || kernel_mask < 1 || kernel_mask > kCatAll) fail("bad arguments");
+    Slot& sl = e->slots[slot];
+    if (!sl.dev_exec[kernel_mask]) sl.dev_exec[kernel_mask] = capture_graph(e, sl.sh, kernel_mask, false, nullptr);
+    while ((int)e->timing_events.size() < iterations + 1) {
+      cudaEvent_t ev;
+      ck(cudaEventCreate(&ev), "event");
+      e->timing_events.push_back(ev);
+    }
+    ck(cudaEventRecord(e->timing_events[0], e->stream), "event");
+    for (int i = 0; i < iterations; ++i) {
+      ck(cudaGraphLaunch(sl.dev_exec[kernel_mask], e->stream), "graph launch");
+      ck(cudaEventRecord(e->timing_events[i + 1], e->stream), "event");
+    }
+    ck(cudaEventSynchronize(e->timing_events[iterations]), "replay");
+    for (int i = 0; i < iterations; ++i)
+      ck(cudaEventElapsedTime(&ms_each[i], e->timing_events[i], e->timing_events[i + 1]), "elapsed");
     if (e->status_host[0]) {
       e->status_host[0] = 0;
       fail("a device-side wait timed out during replay");
     }
-    *ms = t / iterations;
   });
 }
 
@@ -921,6 +968,7 @@ int laya_b200_destroy(laya_b200_engine* e) {
   if (e->h_in) cudaFreeHost(e->h_in);
   if (e->h_out) cudaFreeHost(e->h_out);
   if (e->status_host) cudaFreeHost(e->status_host);
+  for (auto ev : e->timing_events) cudaEventDestroy(ev);
   if (e->ev0) cudaEventDestroy(e->ev0);
   if (e->ev1) cudaEventDestroy(e->ev1);
   if (e->stream) cudaStreamDestroy(e->stream);

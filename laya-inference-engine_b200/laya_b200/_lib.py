@@ -57,7 +57,7 @@ def load():
         "laya_b200_capture": (I, [P, I, I, I, I, ctypes.POINTER(I)]),
         "laya_b200_release": (I, [P, I]),
         "laya_b200_run": (I, [P, I, i64p, i64p, i64p, u8p, i64p, F, F]),
-        "laya_b200_replay_device": (I, [P, I, I, F]),
+        "laya_b200_replay_device": (I, [P, I, I, I, F]),
         "laya_b200_kernel_count": (I, [P, I, ctypes.POINTER(I)]),
         "laya_b200_read_buffer": (I, [P, ctypes.c_char_p, P, ctypes.c_size_t]),
         "laya_b200_last_error": (ctypes.c_char_p, [P]),

@@ -99,11 +99,13 @@ class NativeForward:
         _lib.check(self.lib, self.handle, st, "run")
         return logits, act
 
-    def replay_device(self, slot, iterations):
-        ms = ctypes.c_float()
-        st = self.lib.laya_b200_replay_device(self.handle, slot, iterations, ctypes.byref(ms))
+    def replay_device(self, slot, iterations, kernel_mask=7):
+        """Per-replay device milliseconds of `iterations` back-to-back replays."""
+        ms = np.empty(iterations, dtype=np.float32)
+        st = self.lib.laya_b200_replay_device(self.handle, slot, iterations, kernel_mask,
+                                              ms.ctypes.data_as(ctypes.POINTER(ctypes.c_float)))
         _lib.check(self.lib, self.handle, st, "replay_device")
-        return ms.value
+        return ms
 
     def kernel_count(self, slot):
         n = ctypes.c_int()
