@@ -1,0 +1,334 @@
+"""Benchmark of the b200 Laya forward (one JSON line on rank 0).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
+
+Workload: one short "noul" question, batch 1,
+sequence 64, bf16 weights of the 28x1024 Laya network (seeded random weights,
+synthetic token ids), warm CUDA-graph replay.  A step is one forward = one
+decision.  With N GPUs (torchrun, one process per GPU) every rank serves its
+own stream of requests on its own weight replica (request parallel, no
+collective on the data path; weak scaling); NCCL is used only for the
+barriers and the max-over-ranks of the timed region.
+
+* value: decisions/s of K back-to-back graph replays per rank with inputs
+  resident in HBM, device time from CUDA events on the engine's stream,
+  max over ranks; p50_ms is the median per-replay device time.
+* e2e: the same metric through the public API (B200Engine.run_prepared) with
+  host inputs: pinned H2D of the packed inputs, the graph, D2H of the logits
+  and actions, per step.
+* roofline: the projection GEMM family (the dominant kernel), timed live as a
+  graph of the forward's GEMM launches only; algorithmic bytes = weight bytes
+  + activation bytes each launch must move.
+* cpu_baseline: the CPU oracle port of the reference forward, timed on this
+  host's cores on a bounded sample of the same request.
+"""
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT / "laya-inference-engine_b200"))
+sys.path.insert(0, str(ROOT))
+
+import numpy as np  # noqa: E402
+
+METRIC = "decisions/s at 1/2/4/8 B200 and p50 warm latency, one short question"
+UNIT = "decisions/s"
+FALLBACK_HBM_GBS = 6650.0
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=2000)
+    ap.add_argument("--warmup", type=int, default=50)
+    ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    ap.add_argument("--precision", default="bf16", choices=["bf16", "fp8"])
+    ap.add_argument("--cpu-seconds", type=float, default=15.0)
+    return ap.parse_args()
+
+
+def workload(cfg, seed=0):
+    from laya_b200.workload import synthetic_items, pack
+    items = synthetic_items([64], ["noul"], seed=seed, vocab=cfg.vocab)
+    return items, pack(items, 1, 64, 2, cfg.pad_token_id)
+
+
+def peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return float(d["hbm_gbs"]), "measured"
+    return FALLBACK_HBM_GBS, "fallback"
+
+
+def gemm_bytes(cfg, b, s, k, precision):
+    """Algorithmic bytes of one forward's projection GEMMs: each weight read
+    once (plus fp8 row scales), each activation operand read once, each output
+    written once (a residual epilogue reads and writes fp32)."""
+    T, R, BK = b * s, b * (1 + k), b * k
+    d, I, F = cfg.hidden, cfg.intermediate, cfg.head_ff
+    wb = 1 if precision == "fp8" else 2
+    total, launches = 0, 0
+
+    def g(M, N, K, wbytes, xbytes, obytes):
+        nonlocal total, launches
+        total += N * K * wbytes + M * K * xbytes + M * N * obytes + (N * 4 if wbytes == 1 else 0)
+        launches += 1
+
+    for _ in range(cfg.layers):
+        g(T, 3 * d, d, wb, wb, 2)
+        g(T, d, d, wb, wb, 8)
+        g(T, 2 * I, d, wb, wb, 1)   # GEGLU writes I outputs for 2I rows
+        g(T, d, I, wb, wb, 8)
+    for j in range(cfg.head_layers):
+        rows = R if j == cfg.head_layers - 1 else T
+        g(T, 3 * d, d, 2, 2, 2)
+        g(rows, d, d, 2, 2, 8)
+        g(rows, F, d, 2, 2, 2)
+        g(rows, d, F, 2, 2, 8)
+    g(BK, d, d, 2, 2, 2)
+    return total, launches
+
+
+def forward_bytes(cfg, precision):
+    """Whole-forward algorithmic bytes at batch 1: every matrix weight read
+    once (the survey's bytes_alg: 739,251,200 B in bf16 for the Laya shape)."""
+    d, I, F, A = cfg.hidden, cfg.intermediate, cfg.head_ff, cfg.act_hidden
+    wb = 1 if precision == "fp8" else 2
+    enc = cfg.layers * (3 * d * d + d * d + 2 * I * d + d * I) * wb
+    head = cfg.head_layers * (3 * d * d + 3 * d + d * d + d + F * d + F + d * F + d) * 2
+    tail = (d * d + d + d + 1) * 2 + (A * (d + 4) + A + 2 * A + 2) * 2
+    return enc + head + tail
+
+
+class ClockSampler:
+    """nvidia-smi samples during the timed region (clocks, throttle reasons)."""
+
+    FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+              "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu):
+        self.gpu = gpu
+        self.proc = None
+        self.lines = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except OSError:
+            self.proc = None
+        time.sleep(0.3)
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *_):
+        if self.proc:
+            time.sleep(0.2)
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        sm, mx, reasons = [], None, set()
+        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+        for line in self.lines:
+            parts = [x.strip() for x in line.split(",")]
+            if len(parts) < 8:
+                continue
+            try:
+                sm.append(float(parts[0]))
+                mx = float(parts[1])
+            except ValueError:
+                continue
+            for name, val in zip(names, parts[4:8]):
+                if val.lower().startswith("active"):
+                    reasons.add(name)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def cpu_baseline(cfg, seconds, precision="bf16", max_steps=None):
+    """Time the CPU oracle port of the reference forward on this host."""
+    import torch
+    from laya_b200.weights import seeded_weights
+    from oracle.laya_oracle import Oracle
+    torch.set_num_threads(os.cpu_count() or 1)
+    w = seeded_weights(cfg, seed=0)
+    orc = Oracle(w, cfg, precision)
+    del w
+    _, inp = workload(cfg)
+    orc.forward(**inp)  # warm-up
+    times = []
+    t_end = time.perf_counter() + seconds
+    while time.perf_counter() < t_end and (max_steps is None or len(times) < max_steps):
+        t0 = time.perf_counter()
+        orc.forward(**inp)
+        times.append(time.perf_counter() - t0)
+    total = sum(times)
+    return {"value": len(times) / total, "unit": UNIT, "cores": torch.get_num_threads(), "kind": "port",
+            "sample": f"{len(times)} forwards of b=1 s=64 noul (one decision each), {total:.1f} s, "
+                      f"oracle/laya_oracle.py fp32-with-bf16-rounding restatement on {os.cpu_count()} host cores",
+            "ms_per_forward": 1000 * total / len(times), "steps": len(times)}
+
+
+def dist_setup(n):
+    if n <= 1 and "WORLD_SIZE" not in os.environ:
+        return 0, 1, 0, None
+    import torch
+    import torch.distributed as dist
+    from datetime import timedelta
+    rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
+    local = int(os.environ.get("LOCAL_RANK", rank))
+    torch.cuda.set_device(local)
+    dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=torch.device("cuda", local))
+    return rank, world, local, dist
+
+
+def run_reference(args):
+    rank, world, local, dist = 0, 1, 0, None
+    if "WORLD_SIZE" in os.environ and int(os.environ["WORLD_SIZE"]) > 1:
+        if int(os.environ.get("RANK", "0")) != 0:
+            return 0
+    from laya_b200.config import LAYA
+    budget = max(10.0, min(120.0, args.cpu_seconds * 4))
+    base = cpu_baseline(LAYA, budget, max_steps=args.steps)
+    steps = base["steps"]
+    line = {"metric": METRIC, "value": base["value"], "unit": UNIT, "n_gpus": args.gpus, "steps": steps,
+            "requested_steps": args.steps, "warmup": 1, "ms_per_step": base["ms_per_forward"],
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic", "impl": "reference",
+            "config": {"workload": "C1: b=1, s=64, one noul question (k=2), bf16 weights",
+                       "model": "Laya 28x1024 encoder + 2-layer head, seeded N(0,0.02) weights"},
+            "cpu_baseline": {k: base[k] for k in ("value", "unit", "cores", "kind", "sample")},
+            "e2e": {"value": base["value"], "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        return run_reference(args)
+    if args.warmup < 3:
+        raise SystemExit("--warmup must be at least 3")
+    rank, world, local, dist = dist_setup(args.gpus)
+    import torch
+    from laya_b200.config import LAYA
+    from laya_b200.engine import B200Engine, request_from_items
+    cfg = LAYA
+    eng = B200Engine(config=cfg, device=local, precision=args.precision, max_questions=1, max_options=2,
+                     max_graphs=2)
+    items, inp = workload(cfg, seed=rank)
+    prepared = request_from_items(items)
+    logits, act, meta = eng.run_prepared(prepared)  # captures the graph, inputs now resident
+    slot = eng.graphs[(1, 64, 2, True)]
+    native = eng.native
+    kernels = native.kernel_count(slot)
+    native.replay_device(slot, args.warmup)
+
+    def barrier():
+        if dist:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    def max_over_ranks(x):
+        if not dist:
+            return x
+        t = torch.tensor([x], dtype=torch.float64, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    # ---- device-resident throughput and latency (the value)
+    with ClockSampler(local) as clocks:
+        barrier()
+        ms = native.replay_device(slot, args.steps)
+        barrier()
+    total_ms = max_over_ranks(float(ms.sum()))
+    value = world * args.steps / (total_ms / 1000.0)
+    p50 = float(np.median(ms))
+
+    # ---- end to end through the public API (host buffers, H2D + D2H per step)
+    for _ in range(args.warmup):
+        eng.run_prepared(prepared)
+    e2e_steps = min(args.steps, 2000)
+    barrier()
+    t0 = time.perf_counter()
+    for _ in range(e2e_steps):
+        eng.run_prepared(prepared)
+    e2e_s = max_over_ranks(time.perf_counter() - t0)
+    barrier()
+    e2e_value = world * e2e_steps / e2e_s
+    b, s, k = 1, 64, 2
+    h2d = 4 * (2 * b * s + b + 2 * b * k + 2 * b * (1 + k))
+    d2h = 4 * (b * k + 2 * b)
+
+    # ---- roofline of the dominant kernel family (projection GEMMs)
+    gms = native.replay_device(slot, max(20, min(args.steps, 500)), kernel_mask=1)
+    gemm_ms = float(np.mean(gms))
+    gbytes, glaunch = gemm_bytes(cfg, b, s, k, args.precision)
+    peak, peak_kind = peaks()
+    achieved = gbytes / (gemm_ms / 1000.0) / 1e9
+    fwd_bytes = forward_bytes(cfg, args.precision)
+    fwd_achieved = fwd_bytes / (float(np.mean(ms)) / 1000.0) / 1e9
+    traffic = None
+    tfile = ROOT / "profiles" / f"gemm_{args.precision}_c1_traffic.txt"
+    if tfile.exists():
+        for line in tfile.read_text().splitlines():
+            if line.startswith("traffic_bytes_per_launch:"):
+                traffic = float(line.split(":", 1)[1])
+
+    if rank == 0:
+        base = cpu_baseline(cfg, args.cpu_seconds, args.precision)
+        cs = clocks.summary()
+        line = {
+            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": total_ms / args.steps, "p50_ms": p50,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": args.precision,
+            "data": "synthetic (seeded token ids, seeded N(0,0.02) random-init weights of the 28x1024 Laya shape)",
+            "config": {"workload": "C1: one short noul question, b=1, s=64, k=2, warm CUDA-graph replay",
+                       "model": "Laya: ModernBERT-large-shaped 28x1024 encoder + 2-layer head + scorer",
+                       "global_batch": world, "seq_len": 64,
+                       "parallelism": f"request-parallel replicas x{world} (no collective)",
+                       "l2": f"inputs larger than L2: {fwd_bytes / 1e6:.0f} MB of weights streamed per step"},
+            "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                    "path": "B200Engine.run_prepared -> laya_b200_run (pinned pack, H2D, graph, D2H)"},
+            "roofline": {"bound": "hbm", "kernel": "gemm_kernel (all projection GEMMs of one forward)",
+                         "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                         "traffic": traffic, "peak_source": peak_kind,
+                         "launches_per_forward": glaunch, "algorithmic_bytes_per_launch": gbytes / glaunch,
+                         "avg_launch_us": 1000 * gemm_ms / glaunch},
+            "forward_roofline": {"bytes_alg": fwd_bytes, "achieved_gbs": fwd_achieved,
+                                 "frac": fwd_achieved / peak},
+            "cpu_baseline": {k: base[k] for k in ("value", "unit", "cores", "kind", "sample")},
+            "gpu_launches": kernels * args.steps,
+            "kernels_per_forward": kernels,
+            "clocks": cs,
+        }
+        print(json.dumps(line), flush=True)
+    eng.close()
+    if dist:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())
