@@ -170,6 +170,8 @@ struct laya_b200_engine {
   float* hsel = nullptr;
   __nv_bfloat16 *asel = nullptr, *nsel = nullptr, *fsel = nullptr, *msc = nullptr, *zsc = nullptr;
   float *gcos = nullptr, *gsin = nullptr, *lcos = nullptr, *lsin = nullptr;
+  float* a1 = nullptr;              // tail scratch [max_batch][act_hidden]
+  unsigned int* arrivals = nullptr; // tail arrival counters [max_batch]
   // device inputs / outputs (int32 staging layout)
   int32_t* d_in = nullptr;
   float* d_out = nullptr;
@@ -541,6 +543,8 @@ struct Fwd {
       t.a2_b = wptr<__nv_bfloat16>(e, "act.fc2.b");
       t.logits = E.d_out + L.logits;
       t.act = E.d_out + L.act;
+      t.a1 = E.a1;
+      t.arrivals = E.arrivals;
       count(launch_tail(t, b, st, pdl()), "tail launch");
     }
   }
@@ -677,6 +681,8 @@ int laya_b200_create(int device, const laya_b200_config* cfg, laya_b200_engine**
         {(void**)&e->zsc, BK * d * 2},      {(void**)&e->gcos, (size_t)c.max_len * 64 * 4},
         {(void**)&e->gsin, (size_t)c.max_len * 64 * 4}, {(void**)&e->lcos, (size_t)c.max_len * 64 * 4},
         {(void**)&e->lsin, (size_t)c.max_len * 64 * 4},
+        {(void**)&e->a1, (size_t)c.max_batch * c.act_hidden * 4},
+        {(void**)&e->arrivals, (size_t)c.max_batch * 4},
     };
     size_t aoff = 0;
     for (auto& b : bufs) aoff = align_up(aoff + b.second, 1024);

@@ -43,53 +43,80 @@ struct GemmCfg {
   static constexpr int K_ELEMS = KIND == kKindBf16 ? 64 : 128;
 };
 
+// Epilogue for 4 consecutive weight rows n_lo..n_lo+3 and their partners
+// n_lo+64..n_lo+67 of one token m (lo/hi hold the fp32 accumulators).
 template <int KIND>
-DEVI void epilogue_pair(const GemmParams& p, int m, int n_lo, int geglu_col, float lo, float hi) {
+DEVI void epilogue_quad(const GemmParams& p, int m, int n_lo, int geglu_col, float4 lo, float4 hi) {
+  float l[4] = {lo.x, lo.y, lo.z, lo.w}, h[4] = {hi.x, hi.y, hi.z, hi.w};
   const int n_hi = n_lo + 64;
   if (KIND == kKindFp8) {
     const float sa = p.a_scale[m];
-    lo = (lo * sa) * p.w_scale[n_lo];
-    hi = (hi * sa) * p.w_scale[n_hi];
+    const float4 wl = *reinterpret_cast<const float4*>(p.w_scale + n_lo);
+    const float4 wh = *reinterpret_cast<const float4*>(p.w_scale + n_hi);
+    const float wlv[4] = {wl.x, wl.y, wl.z, wl.w}, whv[4] = {wh.x, wh.y, wh.z, wh.w};
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      l[e] = (l[e] * sa) * wlv[e];
+      h[e] = (h[e] * sa) * whv[e];
+    }
   } else if (KIND == kKindNvfp4) {
     const float sa = p.a_scale[m] * p.w_tensor_scale;
-    lo *= sa;
-    hi *= sa;
-  }
-  switch (p.epilogue) {
-    case kEpiGeglu: {
-      const float a = bf16_round(lo), g = bf16_round(hi);
-      const float ge = bf16_round(gelu_erf(a));
-      p.out[(size_t)m * p.ldo + geglu_col] = __float2bfloat16_rn(ge * g);
-      break;
-    }
-    case kEpiResidual: {
-      if (p.bias) {
-        lo += __bfloat162float(p.bias[n_lo]);
-        hi += __bfloat162float(p.bias[n_hi]);
-      }
-      float* r = p.resid + (size_t)m * p.ldr;
-      r[n_lo] = r[n_lo] + bf16_round(lo);
-      r[n_hi] = r[n_hi] + bf16_round(hi);
-      break;
-    }
-    default: {
-      if (p.bias) {
-        lo += __bfloat162float(p.bias[n_lo]);
-        hi += __bfloat162float(p.bias[n_hi]);
-      }
-      if (p.epilogue == kEpiRelu) {
-        lo = fmaxf(lo, 0.f);
-        hi = fmaxf(hi, 0.f);
-      } else if (p.epilogue == kEpiGelu) {
-        lo = gelu_erf(bf16_round(lo));
-        hi = gelu_erf(bf16_round(hi));
-      }
-      __nv_bfloat16* o = p.out + (size_t)m * p.ldo;
-      o[n_lo] = __float2bfloat16_rn(lo);
-      o[n_hi] = __float2bfloat16_rn(hi);
-      break;
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      l[e] *= sa;
+      h[e] *= sa;
     }
   }
+  if (p.epilogue == kEpiGeglu) {
+    __nv_bfloat16 o[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float a = bf16_round(l[e]), g = bf16_round(h[e]);
+      o[e] = __float2bfloat16_rn(bf16_round(gelu_erf(a)) * g);
+    }
+    *reinterpret_cast<uint2*>(p.out + (size_t)m * p.ldo + geglu_col) = *reinterpret_cast<uint2*>(o);
+    return;
+  }
+  if (p.bias) {
+    const uint2 bl = *reinterpret_cast<const uint2*>(p.bias + n_lo);
+    const uint2 bh = *reinterpret_cast<const uint2*>(p.bias + n_hi);
+    const __nv_bfloat16* bla = reinterpret_cast<const __nv_bfloat16*>(&bl);
+    const __nv_bfloat16* bha = reinterpret_cast<const __nv_bfloat16*>(&bh);
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      l[e] += __bfloat162float(bla[e]);
+      h[e] += __bfloat162float(bha[e]);
+    }
+  }
+  if (p.epilogue == kEpiResidual) {
+    float4* rl = reinterpret_cast<float4*>(p.resid + (size_t)m * p.ldr + n_lo);
+    float4* rh = reinterpret_cast<float4*>(p.resid + (size_t)m * p.ldr + n_hi);
+    float4 a = *rl, b = *rh;
+    a.x += bf16_round(l[0]); a.y += bf16_round(l[1]); a.z += bf16_round(l[2]); a.w += bf16_round(l[3]);
+    b.x += bf16_round(h[0]); b.y += bf16_round(h[1]); b.z += bf16_round(h[2]); b.w += bf16_round(h[3]);
+    *rl = a;
+    *rh = b;
+    return;
+  }
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+    if (p.epilogue == kEpiRelu) {
+      l[e] = fmaxf(l[e], 0.f);
+      h[e] = fmaxf(h[e], 0.f);
+    } else if (p.epilogue == kEpiGelu) {
+      l[e] = gelu_erf(bf16_round(l[e]));
+      h[e] = gelu_erf(bf16_round(h[e]));
+    }
+  }
+  __nv_bfloat16 ol[4], oh[4];
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+    ol[e] = __float2bfloat16_rn(l[e]);
+    oh[e] = __float2bfloat16_rn(h[e]);
+  }
+  __nv_bfloat16* o = p.out + (size_t)m * p.ldo;
+  *reinterpret_cast<uint2*>(o + n_lo) = *reinterpret_cast<uint2*>(ol);
+  *reinterpret_cast<uint2*>(o + n_hi) = *reinterpret_cast<uint2*>(oh);
 }
 
 template <int BN, int KIND, int STAGES>
@@ -217,29 +244,35 @@ __global__ void __launch_bounds__(128, 1)
   else
     __syncthreads();
 
-  // ---- reduction over the cluster and the epilogue
-  const int j0 = rank * 64 / split, j1 = (rank + 1) * 64 / split, np = j1 - j0;
+  // ---- reduction over the cluster and the epilogue.  CTA `rank` owns the
+  // tokens [t0, t1) of the tile; a thread takes 4 consecutive rows (and their
+  // +64 partners) of one token and sums the S partials in rank order with
+  // 16-byte DSMEM loads issued back to back.
+  const int t0 = rank * BN / split, t1 = (rank + 1) * BN / split, nt = t1 - t0;
   const uint32_t part_addr = smem_u32(part);
-  for (int idx = tid; idx < np * BN; idx += 128) {
-    const int jj = j0 + idx % np;
-    const int ml = idx / np;
-    const int m = tile_m * BN + ml;
+  for (int item = tid; item < nt * 16; item += 128) {
+    const int tl = t0 + (item >> 4);
+    const int q4 = (item & 15) * 4;
+    const int m = tile_m * BN + tl;
     if (m >= p.M) continue;
-    const int off = ml * 128 + jj;
-    float lo, hi;
+    const int off = tl * 128 + q4;
+    float4 lo, hi;
     if (split == 1) {
-      lo = part[off];
-      hi = part[off + 64];
+      lo = *reinterpret_cast<const float4*>(part + off);
+      hi = *reinterpret_cast<const float4*>(part + off + 64);
     } else {
-      lo = 0.f;
-      hi = 0.f;
+      lo = make_float4(0.f, 0.f, 0.f, 0.f);
+      hi = lo;
+#pragma unroll 4
       for (int q = 0; q < split; ++q) {
         const uint32_t base = mapa_shared(part_addr, (uint32_t)q);
-        lo += ld_dsmem_f32(base + off * 4);
-        hi += ld_dsmem_f32(base + (off + 64) * 4);
+        const float4 a = ld_dsmem_f32x4(base + off * 4);
+        const float4 b = ld_dsmem_f32x4(base + (off + 64) * 4);
+        lo.x += a.x; lo.y += a.y; lo.z += a.z; lo.w += a.w;
+        hi.x += b.x; hi.y += b.y; hi.z += b.z; hi.w += b.w;
       }
     }
-    epilogue_pair<KIND>(p, m, tile_n * 128 + jj, tile_n * 64 + jj, lo, hi);
+    epilogue_quad<KIND>(p, m, tile_n * 128 + q4, tile_n * 64 + q4, lo, hi);
   }
   if (split > 1) cluster_sync_all();
 

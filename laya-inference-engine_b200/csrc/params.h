@@ -102,6 +102,8 @@ struct TailParams {
   const __nv_bfloat16* a2_b;
   float* logits;             // [b][k]
   float* act;                // [b][2]
+  float* a1;                 // scratch [b][act_hidden]: act_head layer-1 outputs
+  unsigned int* arrivals;    // [b] CTA arrival counters, zero between launches
 };
 
 }  // namespace laya

@@ -168,27 +168,39 @@ __global__ void __launch_bounds__(256) gather_rows_kernel(float* dst, const floa
   for (int c = lane; c < d / 4; c += 32) o[c] = s[c];
 }
 
-// One CTA per question: logits, softmax features and act_head (model.py:113-122).
+// Decision tail (model.py:113-122).  Grid (questions, kTailCtas): every CTA
+// recomputes the question's logits and softmax features (cheap) and a slice
+// of act_head's first layer; the last CTA of a question to finish (atomic
+// arrival count, no spinning) applies the second layer and resets the count.
+constexpr int kTailCtas = 16;
+
 __global__ void __launch_bounds__(256) tail_kernel(const TailParams p) {
   extern __shared__ float tsm[];
   float* s_logit = tsm;                       // [k]
   float* s_x = tsm + 256;                     // [d + 4] (bf16-rounded act_head input)
-  float* s_a1 = s_x + p.d + 8;                // [act_hidden]
+  __shared__ unsigned int s_last;
   griddep_launch_dependents();
   griddep_wait();
-  const int q = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nw = blockDim.x >> 5;
+  const int q = blockIdx.x, part = blockIdx.y, nparts = gridDim.y;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nw = blockDim.x >> 5;
   // scorer[3]: logit_j = bf16(z_j . w + b), masked to -1e4
   for (int j = warp; j < p.k; j += nw) {
     const __nv_bfloat16* z = p.z + ((size_t)q * p.k + j) * p.d;
     float acc = 0.f;
-    for (int c = lane; c < p.d; c += 32) acc += __bfloat162float(z[c]) * __bfloat162float(p.fc2_w[c]);
+    for (int c = lane * 8; c < p.d; c += 256) {
+      const uint4 zu = *reinterpret_cast<const uint4*>(z + c);
+      const uint4 wu = *reinterpret_cast<const uint4*>(p.fc2_w + c);
+      const __nv_bfloat16* za = reinterpret_cast<const __nv_bfloat16*>(&zu);
+      const __nv_bfloat16* wa = reinterpret_cast<const __nv_bfloat16*>(&wu);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) acc += __bfloat162float(za[e]) * __bfloat162float(wa[e]);
+    }
     acc = warp_sum(acc);
     if (lane == 0) {
       const float l = bf16_round(acc + __bfloat162float(p.fc2_b[0]));
       s_logit[j] = p.marker_mask[q * p.k + j] ? l : -1e4f;
     }
   }
-  // CLS row of the selected hidden states
   const float* cls = p.h_sel + (size_t)q * (1 + p.k) * p.d;
   for (int c = tid; c < p.d; c += blockDim.x) s_x[c] = bf16_round(cls[c]);
   __syncthreads();
@@ -211,7 +223,7 @@ __global__ void __launch_bounds__(256) tail_kernel(const TailParams p) {
       } else if (pj > t2) {
         t2 = pj;
       }
-      p.logits[q * p.k + j] = s_logit[j];
+      if (part == 0) p.logits[q * p.k + j] = s_logit[j];
     }
     const float cnt = (float)(count < 2 ? 2 : count);
     ent = -ent / logf(cnt);
@@ -221,24 +233,33 @@ __global__ void __launch_bounds__(256) tail_kernel(const TailParams p) {
     s_x[p.d + 3] = bf16_round(cnt / 255.0f);
   }
   __syncthreads();
-  // act_head[0..1]: a1 = bf16(gelu(bf16(W1 x + b1)))
+  // act_head[0..1] for this CTA's slice: a1 = bf16(gelu(bf16(W1 x + b1)))
   const int din = p.d + 4;
-  for (int u = warp; u < p.act_hidden; u += nw) {
+  const int per = (p.act_hidden + nparts - 1) / nparts;
+  const int u0 = part * per, u1 = min(p.act_hidden, u0 + per);
+  for (int u = u0 + warp; u < u1; u += nw) {
     const __nv_bfloat16* wr = p.a1_w + (size_t)u * din;
     float acc = 0.f;
     for (int c = lane; c < din; c += 32) acc += __bfloat162float(wr[c]) * s_x[c];
     acc = warp_sum(acc);
-    if (lane == 0) s_a1[u] = bf16_round(gelu_erf(bf16_round(acc + __bfloat162float(p.a1_b[u]))));
+    if (lane == 0) p.a1[(size_t)q * p.act_hidden + u] = bf16_round(gelu_erf(bf16_round(acc + __bfloat162float(p.a1_b[u]))));
   }
+  __threadfence();
   __syncthreads();
+  if (tid == 0) s_last = atomicAdd(&p.arrivals[q], 1u) == (unsigned)(nparts - 1);
+  __syncthreads();
+  if (!s_last) return;
+  __threadfence();
   // act_head[2]: act = bf16(W2 a1 + b2)
   if (warp < 2) {
     const __nv_bfloat16* wr = p.a2_w + (size_t)warp * p.act_hidden;
+    const float* a1 = p.a1 + (size_t)q * p.act_hidden;
     float acc = 0.f;
-    for (int c = lane; c < p.act_hidden; c += 32) acc += __bfloat162float(wr[c]) * s_a1[c];
+    for (int c = lane; c < p.act_hidden; c += 32) acc += __bfloat162float(wr[c]) * __ldcg(a1 + c);
     acc = warp_sum(acc);
     if (lane == 0) p.act[q * 2 + warp] = bf16_round(acc + __bfloat162float(p.a2_b[warp]));
   }
+  if (tid == 0) p.arrivals[q] = 0;
 }
 
 // Per-output-row e4m3 weight quantisation (quantization.py:62-73), bf16 in.
@@ -319,9 +340,9 @@ cudaError_t launch_tail(const TailParams& p, int batch, cudaStream_t stream, boo
   TailParams q = p;
   void* args[] = {&q};
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(batch, 1, 1);
+  cfg.gridDim = dim3(batch, kTailCtas, 1);
   cfg.blockDim = dim3(256, 1, 1);
-  cfg.dynamicSmemBytes = (256 + p.d + 8 + p.act_hidden) * sizeof(float);
+  cfg.dynamicSmemBytes = (256 + p.d + 8) * sizeof(float);
   cfg.stream = stream;
   cudaLaunchAttribute attr;
   attr.id = cudaLaunchAttributeProgrammaticStreamSerialization;
