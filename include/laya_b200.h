@@ -96,6 +96,42 @@ LAYA_B200_API int laya_b200_kernel_count(laya_b200_engine* e, int slot, int* cou
  * compare intermediate results with a CPU oracle. */
 LAYA_B200_API int laya_b200_read_buffer(laya_b200_engine* e, const char* name, void* dst, size_t bytes);
 
+/* Arguments of laya_b200_tail_noalloc: device pointers the caller owns. */
+typedef struct laya_b200_tail_args {
+  int32_t questions;         /* 1..64 */
+  int32_t options;           /* padded option count k, 2..256 */
+  int32_t hidden;            /* d */
+  int32_t act_hidden;        /* act_head width; questions * act_hidden <= 65536 */
+  const void* z;             /* bf16 [questions*options][hidden]: gelu(scorer.fc1) of the option rows */
+  const void* fc2_w;         /* bf16 [hidden]: scorer.fc2 weight */
+  const void* fc2_b;         /* bf16 [1] */
+  const int32_t* marker_mask;/* int32 [questions][options], nonzero = real option */
+  const float* h_sel;        /* fp32 [questions*(1+options)][hidden]: CLS row then option rows */
+  const void* a1_w;          /* bf16 [act_hidden][hidden+4]: act_head[0] */
+  const void* a1_b;          /* bf16 [act_hidden] */
+  const void* a2_w;          /* bf16 [2][act_hidden]: act_head[2] */
+  const void* a2_b;          /* bf16 [2] */
+  float* logits;             /* out fp32 [questions][options], masked options = -1e4 */
+  float* act;                /* out fp32 [questions][2] */
+} laya_b200_tail_args;
+
+/* No counterpart in the reference.  The decision tail (scorer logits, masked
+ * softmax features, act_head) for callers that cannot allocate device memory
+ * -- a host that owns every device buffer through its own allocator or pool,
+ * or a worker restricted to launching on memory it was handed.  It calls no
+ * cudaMalloc, cudaFree or allocating library routine: its scratch lives in a
+ * fixed 256 KiB file-scope __device__ array that every GPU loading this
+ * library keeps until process exit, which limits a call to 64 questions and
+ * questions * act_hidden <= 65536; larger calls are rejected.  The first call
+ * on a device looks up that array's device address (once per device, with
+ * the device current), so make it before any stream capture.  All calls on a
+ * device share the array and it keeps the last call's contents; the call
+ * clears its counters itself, and calls whose kernels overlap on the GPU
+ * race.  `stream` is a cudaStream_t (NULL: the legacy default stream); the
+ * launch is asynchronous.  Errors: nonzero return, message from
+ * laya_b200_last_error(NULL) on the calling thread. */
+LAYA_B200_API int laya_b200_tail_noalloc(const laya_b200_tail_args* args, void* stream);
+
 /* Last error message of the engine (or of the last failed create when e is
  * NULL).  The pointer stays valid until the next call on the engine. */
 LAYA_B200_API const char* laya_b200_last_error(laya_b200_engine* e);

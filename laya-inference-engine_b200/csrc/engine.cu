@@ -26,8 +26,15 @@
 using namespace laya;
 
 namespace {
-
 thread_local std::string g_create_error;
+}  // namespace
+
+namespace laya {
+// Message of the last failed engine-less call on this thread (create, tail).
+std::string& create_error_message() { return g_create_error; }
+}  // namespace laya
+
+namespace {
 
 typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,

@@ -14,7 +14,7 @@ PRECISIONS = {"bf16": 0, "fp8": 1, "nvfp4": 2}
 
 EXPORTS = ("laya_b200_create", "laya_b200_set_weight", "laya_b200_finalize", "laya_b200_capture",
            "laya_b200_release", "laya_b200_run", "laya_b200_replay_device", "laya_b200_kernel_count",
-           "laya_b200_read_buffer", "laya_b200_last_error", "laya_b200_destroy")
+           "laya_b200_read_buffer", "laya_b200_tail_noalloc", "laya_b200_last_error", "laya_b200_destroy")
 
 
 class Config(ctypes.Structure):
@@ -23,6 +23,13 @@ class Config(ctypes.Structure):
                [(n, ctypes.c_float) for n in ("rope_theta_global", "rope_theta_local", "norm_eps")] + \
                [(n, ctypes.c_int32) for n in ("head_layers", "head_heads", "head_ff", "num_qtypes", "act_hidden",
                                                 "max_batch", "max_options")]
+
+
+class TailArgs(ctypes.Structure):
+    """laya_b200_tail_args: device pointers owned by the caller."""
+    _fields_ = [(n, ctypes.c_int32) for n in ("questions", "options", "hidden", "act_hidden")] + \
+               [(n, ctypes.c_void_p) for n in ("z", "fc2_w", "fc2_b", "marker_mask", "h_sel", "a1_w", "a1_b",
+                                                "a2_w", "a2_b", "logits", "act")]
 
 
 def make_config(cfg, max_batch, max_options):
@@ -60,6 +67,7 @@ def load():
         "laya_b200_replay_device": (I, [P, I, I, I, F]),
         "laya_b200_kernel_count": (I, [P, I, ctypes.POINTER(I)]),
         "laya_b200_read_buffer": (I, [P, ctypes.c_char_p, P, ctypes.c_size_t]),
+        "laya_b200_tail_noalloc": (I, [ctypes.POINTER(TailArgs), P]),
         "laya_b200_last_error": (ctypes.c_char_p, [P]),
         "laya_b200_destroy": (I, [P]),
     }
