@@ -1,0 +1,172 @@
+"""Request-parallel dispatch of decision questions over 1-8 GPUs of one node.
+
+The reference serves one GPU per engine behind a lock
+(``src/laya_blackwell/engine.py:84,192``) and has no multi-GPU path; its
+multi-stream ``StreamService`` prototype (``experiments/latency/serving``)
+overlaps independent requests.  Here every GPU holds its own weight replica,
+CUDA graphs and pinned buffers (one ``B200Engine`` per device, driven by its
+own worker thread: ctypes releases the GIL inside the native forward), and
+independent questions are partitioned across GPUs:
+
+* each question is priced at its bucketed token count (sequence bucket x 1);
+* questions are assigned longest-first to the least-loaded GPU (LPT);
+* on each GPU, questions that share a sequence bucket run as one batched
+  forward (batch padded to a power of two, as ``BlackwellEngine._shape``).
+
+There is no collective anywhere: results return to the caller's thread.
+Failure handling is on the host: a worker that raises or exceeds ``timeout``
+marks its GPU unhealthy, and its questions are re-run on the healthy GPUs
+(``retry=True``) or reported as errors.
+"""
+from concurrent.futures import ThreadPoolExecutor, TimeoutError as FutureTimeout
+import threading
+
+import numpy as np
+
+from .engine import request_from_items
+
+
+def bucket_of(length, buckets):
+    for b in buckets:
+        if length <= b:
+            return b
+    raise ValueError(f"sequence of {length} tokens exceeds the largest bucket {buckets[-1]}")
+
+
+def lpt_partition(costs, parts):
+    """Longest-processing-time-first assignment of items to `parts` bins.
+
+    Deterministic (ties broken by item index, then bin index), so every rank of
+    a multi-process job computes the same partition without communicating.
+    Returns a list of index lists, one per bin."""
+    if parts < 1:
+        raise ValueError("parts must be positive")
+    order = sorted(range(len(costs)), key=lambda i: (-costs[i], i))
+    load = [0] * parts
+    bins = [[] for _ in range(parts)]
+    for i in order:
+        j = min(range(parts), key=lambda p: (load[p], p))
+        bins[j].append(i)
+        load[j] += costs[i]
+    for b in bins:
+        b.sort()
+    return bins
+
+
+def group_by_bucket(items, indices, buckets, max_batch):
+    """Batches of item indices that share a sequence bucket (<= max_batch each)."""
+    groups = {}
+    for i in indices:
+        groups.setdefault(bucket_of(len(items[i]["ids"]), buckets), []).append(i)
+    out = []
+    for bucket in sorted(groups):
+        idx = groups[bucket]
+        for s in range(0, len(idx), max_batch):
+            out.append((bucket, idx[s:s + max_batch]))
+    return out
+
+
+class B200Dispatcher:
+    """Serve independent questions on several GPUs, one engine replica each."""
+
+    def __init__(self, devices=(0,), *, engine_factory=None, timeout=None, retry=True,
+                 sequence_buckets=tuple(range(32, 513, 32)), max_batch=64, **engine_kwargs):
+        if not devices:
+            raise ValueError("at least one device is required")
+        self.devices = list(devices)
+        self.timeout, self.retry = timeout, retry
+        self.buckets = tuple(sorted(sequence_buckets))
+        self.max_batch = max_batch
+        if engine_factory is None:
+            from .engine import B200Engine
+
+            def engine_factory(device, **kw):
+                return B200Engine(device=device, sequence_buckets=self.buckets, max_questions=max_batch, **kw)
+        self.engines = {}
+        with ThreadPoolExecutor(max_workers=len(self.devices)) as ex:
+            futs = {d: ex.submit(engine_factory, d, **engine_kwargs) for d in self.devices}
+            for d, f in futs.items():
+                self.engines[d] = f.result()
+        self.pools = {d: ThreadPoolExecutor(max_workers=1, thread_name_prefix=f"laya-gpu{d}")
+                      for d in self.devices}
+        self.healthy = {d: True for d in self.devices}
+        self.lock = threading.Lock()
+        self.closed = False
+
+    def _run_batches(self, device, items, batches):
+        eng = self.engines[device]
+        out = {}
+        for _, idx in batches:
+            logits, act, _ = eng.run_prepared(request_from_items([items[i] for i in idx]))
+            for row, i in enumerate(idx):
+                k = len(items[i]["markers"])
+                out[i] = (logits[row, :max(k, 1)].copy(), act[row].copy())
+        return out
+
+    def run_items(self, items):
+        """Logits [k_i] and act [2] per item, in input order.
+
+        Raises RuntimeError when an item could not be served on any GPU."""
+        if self.closed:
+            raise RuntimeError("Dispatcher is closed")
+        if not items:
+            return []
+        results = {}
+        pending = list(range(len(items)))
+        errors = {}
+        while pending:
+            with self.lock:
+                alive = [d for d in self.devices if self.healthy[d]]
+            if not alive:
+                raise RuntimeError(f"no healthy GPU left; {len(pending)} questions unserved: {errors}")
+            costs = [bucket_of(len(items[i]["ids"]), self.buckets) for i in pending]
+            shards = lpt_partition(costs, len(alive))
+            futs = {}
+            for d, shard in zip(alive, shards):
+                idx = [pending[j] for j in shard]
+                if idx:
+                    futs[d] = (idx, self.pools[d].submit(self._run_batches, d, items,
+                                                         group_by_bucket(items, idx, self.buckets, self.max_batch)))
+            failed = []
+            for d, (idx, fut) in futs.items():
+                try:
+                    results.update(fut.result(timeout=self.timeout))
+                except (Exception, FutureTimeout) as exc:  # noqa: BLE001 - any worker failure
+                    with self.lock:
+                        self.healthy[d] = False
+                    errors[d] = repr(exc)
+                    failed.extend(idx)
+            if failed and not self.retry:
+                raise RuntimeError(f"GPU worker failures: {errors}")
+            pending = sorted(failed)
+        return [results[i] for i in range(len(items))]
+
+    def close(self):
+        if self.closed:
+            return
+        self.closed = True
+        for p in self.pools.values():
+            p.shutdown(wait=True)
+        for e in self.engines.values():
+            e.close()
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *_):
+        self.close()
+
+
+def shard_for_rank(items, world, rank, buckets=tuple(range(32, 513, 32))):
+    """The items one rank of a multi-process job serves (same LPT on every rank)."""
+    costs = [bucket_of(len(it["ids"]), buckets) for it in items]
+    return lpt_partition(costs, world)[rank]
+
+
+def c4_step(seed, vocab, questions=64, lo=32, hi=512):
+    """`questions` questions, lengths uniform in [lo, hi],
+    seeded mix of question types."""
+    from .workload import synthetic_items, mixed_kinds
+    rng = np.random.Generator(np.random.PCG64(seed))
+    lengths = rng.integers(lo, hi + 1, size=questions).tolist()
+    return synthetic_items(lengths, mixed_kinds(questions, seed), seed=seed, vocab=vocab)

@@ -1,0 +1,157 @@
+"""B200Engine shape, graph-key, fill and lifetime semantics without CUDA,
+mirroring the reference's tests/test_engine_cpu.py tables."""
+from collections import OrderedDict
+import threading
+
+import numpy as np
+import pytest
+
+from laya_b200.config import TINY
+from laya_b200.engine import B200Engine, request_from_items, _device_index
+from laya_b200.protocol import PreparedRequest
+from laya_b200.workload import pack
+
+
+class FakeNative:
+    def __init__(self):
+        self.captured, self.released, self.runs = [], [], 0
+        self.closed = False
+
+    def capture(self, b, s, k, unmasked):
+        self.captured.append((b, s, k, unmasked))
+        return len(self.captured) - 1
+
+    def release(self, slot):
+        self.released.append(slot)
+
+    def run(self, slot, inputs):
+        self.runs += 1
+        b, k = inputs["marker_pos"].shape
+        return np.full((b, k), float(slot), np.float32), np.zeros((b, 2), np.float32)
+
+    def close(self):
+        self.closed = True
+
+
+def make_engine(*, max_questions=64, max_len=512, max_graphs=8):
+    engine = B200Engine.__new__(B200Engine)
+    engine.lock = threading.RLock()
+    engine.max_questions, engine.max_graphs = max_questions, max_graphs
+    engine.sequence_buckets = (64, 128, 256, 384, 512, 768, 1024)
+    engine.cfg = {"max_len": max_len}
+    engine.pad_token_id = 0
+    engine.max_options = 256
+    engine.backend, engine.precision, engine.device = "b200-bf16", "bf16", 0
+    engine.graphs = OrderedDict()
+    engine.closed = False
+    engine.native = FakeNative()
+    return engine
+
+
+def request_with_shapes(*shapes):
+    items = [{"ids": [10] * length, "markers": list(range(options)), "qtype": index % 3}
+             for index, (length, options) in enumerate(shapes)]
+    return PreparedRequest([str(i) for i in range(len(items))], [{}] * len(items), items,
+                           sum(len(item["ids"]) for item in items))
+
+
+@pytest.mark.parametrize("shapes, limit, max_len, expected", [
+    ([(1, 1)], 64, 512, (1, 64, 2)),
+    ([(65, 3)], 64, 512, (1, 128, 4)),
+    ([(65, 3), (80, 2), (20, 1)], 64, 512, (4, 128, 4)),
+    ([(20, 2)] * 5, 6, 512, (6, 64, 2)),
+    ([(80, 2)], 64, 96, (1, 96, 2)),
+    ([(512, 65)], 64, 512, (1, 512, 128)),
+])
+def test_shape_buckets_match_reference_table(shapes, limit, max_len, expected):
+    engine = make_engine(max_questions=limit, max_len=max_len)
+    assert engine._shape(request_with_shapes(*shapes)) == expected
+
+
+@pytest.mark.parametrize("shapes, unmasked", [
+    ([(64, 2)], True), ([(63, 2)], False), ([(64, 2), (64, 2)], True),
+    ([(64, 2), (63, 2)], False), ([(64, 2)] * 3, False),
+])
+def test_graph_key_separates_unmasked(shapes, unmasked):
+    engine = make_engine()
+    prepared = request_with_shapes(*shapes)
+    assert engine._graph_key(prepared) == (*engine._shape(prepared), unmasked)
+
+
+def test_fill_pads_dummy_rows_like_the_reference():
+    prepared = request_with_shapes((3, 2), (2, 1))
+    prepared.items[0]["ids"] = [1, 3, 2]
+    prepared.items[1]["ids"] = [1, 2]
+    buf = pack(prepared.items, 4, 8, 4, 0)
+    assert buf["input_ids"].tolist() == [[1, 3, 2, 0, 0, 0, 0, 0], [1, 2, 0, 0, 0, 0, 0, 0], [0] * 8, [0] * 8]
+    assert buf["attention_mask"].tolist() == [[1, 1, 1, 0, 0, 0, 0, 0], [1, 1, 0, 0, 0, 0, 0, 0],
+                                              [1, 0, 0, 0, 0, 0, 0, 0], [1, 0, 0, 0, 0, 0, 0, 0]]
+    assert buf["marker_pos"].tolist() == [[0, 1, 0, 0], [0] * 4, [0] * 4, [0] * 4]
+    assert buf["marker_mask"].tolist() == [[True, True, False, False], [True, False, False, False],
+                                           [True, False, False, False], [True, False, False, False]]
+    assert buf["qtype"].tolist() == [0, 1, 0, 0]
+
+
+def test_closed_engine_rejects_requests():
+    engine = make_engine()
+    engine.closed = True
+    with pytest.raises(RuntimeError, match="Engine is closed"):
+        engine.run_prepared(request_with_shapes())
+
+
+def test_empty_request_creates_no_graph():
+    engine = make_engine()
+    logits, act, metrics = engine.run_prepared(request_with_shapes())
+    assert logits.shape == (0, 0) and act.shape == (0, 2) and metrics["graph_miss"] is False
+    assert not engine.graphs and not engine.native.captured
+
+
+def test_graph_cache_hits_and_lru_eviction_release_slots():
+    engine = make_engine(max_graphs=2)
+    a, b, c = request_with_shapes((64, 2)), request_with_shapes((100, 2)), request_with_shapes((300, 4))
+    assert engine.run_prepared(a)[2]["graph_miss"] is True
+    assert engine.run_prepared(a)[2]["graph_miss"] is False
+    engine.run_prepared(b)
+    engine.run_prepared(c)           # evicts a's slot
+    assert engine.native.released == [0]
+    assert list(engine.graphs) == [(1, 128, 2, False), (1, 384, 4, False)]
+    assert engine.run_prepared(a)[2]["graph_miss"] is True
+
+
+def test_outputs_are_owned_copies_and_metrics_have_reference_keys():
+    engine = make_engine()
+    logits, act, metrics = engine.run_prepared(request_with_shapes((64, 2), (10, 2), (5, 2)))
+    assert logits.shape == (3, 2) and act.shape == (3, 2)
+    assert logits.base is None or logits.base is not engine.native
+    assert {"graph_miss", "graph_build_ms", "shape", "backend"} <= set(metrics)
+    assert metrics["shape"] == [4, 64, 2]
+
+
+def test_oversized_questions_are_rejected_before_device_work():
+    engine = make_engine(max_len=96)
+    with pytest.raises(ValueError, match="tokens"):
+        engine.run_prepared(request_with_shapes((97, 2)))
+    assert engine.native.runs == 0
+
+
+def test_close_is_idempotent_and_releases_native():
+    engine = make_engine()
+    native = engine.native
+    engine.close()
+    engine.close()
+    assert native.closed and engine.closed and engine.native is None
+
+
+def test_constructor_validation_happens_before_native_work():
+    with pytest.raises(ValueError, match="positive"):
+        B200Engine(max_graphs=0)
+    with pytest.raises(ValueError, match="precision"):
+        B200Engine(precision="int4")
+    with pytest.raises(RuntimeError, match="CUDA devices only"):
+        _device_index("cpu")
+
+
+def test_request_from_items_counts_tokens():
+    items = [{"ids": [1, 2, 3], "markers": [1, 2], "qtype": 0}, {"ids": [4], "markers": [0, 0], "qtype": 2}]
+    req = request_from_items(items)
+    assert req.input_tokens == 4 and len(req.ids) == 2
