@@ -305,14 +305,16 @@ struct Fwd {
   void gemm(const Proj& w, const void* x, const float* x_scale, int M, int epi, __nv_bfloat16* out, int ldo,
             float* resid, int ldr) {
     if (!on(kCatGemm)) return;
-    const int bn = gemm_token_tile(M);
+    const int kb = (w.K + gemm_k_elems(w.kind) - 1) / gemm_k_elems(w.kind);
+    int bn = 0, split = 1;
+    gemm_plan(M, w.N, kb, e->sm_count, &bn, &split);
     const int esize = w.kind == kKindBf16 ? 2 : 1;
     CUtensorMap xmap = make_map(x, M, w.K, esize, bn);
     GemmParams p{};
     p.M = M;
     p.N = w.N;
     p.K = w.K;
-    p.kblocks = (w.K + gemm_k_elems(w.kind) - 1) / gemm_k_elems(w.kind);
+    p.kblocks = kb;
     p.epilogue = epi;
     p.out = out;
     p.ldo = ldo;
@@ -322,8 +324,6 @@ struct Fwd {
     p.a_scale = x_scale;
     p.w_scale = w.w_scale;
     p.status = e->status_dev;
-    const int tiles = (w.N / 128) * ((M + bn - 1) / bn);
-    const int split = gemm_split(tiles, p.kblocks, e->sm_count, 8);
     count(launch_gemm(w.kind, w.map, xmap, p, bn, split, st, pdl()), "gemm launch");
   }
 

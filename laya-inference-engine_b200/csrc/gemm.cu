@@ -263,13 +263,22 @@ __global__ void __launch_bounds__(128, 1)
     } else {
       lo = make_float4(0.f, 0.f, 0.f, 0.f);
       hi = lo;
-#pragma unroll 4
-      for (int q = 0; q < split; ++q) {
-        const uint32_t base = mapa_shared(part_addr, (uint32_t)q);
-        const float4 a = ld_dsmem_f32x4(base + off * 4);
-        const float4 b = ld_dsmem_f32x4(base + (off + 64) * 4);
-        lo.x += a.x; lo.y += a.y; lo.z += a.z; lo.w += a.w;
-        hi.x += b.x; hi.y += b.y; hi.z += b.z; hi.w += b.w;
+      // all remote loads of up to 8 peers are issued before any add
+      for (int q0 = 0; q0 < split; q0 += 8) {
+        float4 va[8], vb[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u)
+          if (q0 + u < split) {
+            const uint32_t base = mapa_shared(part_addr, (uint32_t)(q0 + u));
+            va[u] = ld_dsmem_f32x4(base + off * 4);
+            vb[u] = ld_dsmem_f32x4(base + (off + 64) * 4);
+          }
+#pragma unroll
+        for (int u = 0; u < 8; ++u)
+          if (q0 + u < split) {
+            lo.x += va[u].x; lo.y += va[u].y; lo.z += va[u].z; lo.w += va[u].w;
+            hi.x += vb[u].x; hi.y += vb[u].y; hi.z += vb[u].z; hi.w += vb[u].w;
+          }
       }
     }
     epilogue_quad<KIND>(p, m, tile_n * 128 + q4, tile_n * 64 + q4, lo, hi);
@@ -348,6 +357,23 @@ cudaError_t dispatch_bn(int bn, const CUtensorMap& wmap, const CUtensorMap& xmap
 }
 
 }  // namespace
+
+// Token tile and split-K factor for one projection.  Small token counts use
+// one token tile of the smallest MMA width that covers them and split K over
+// a cluster until about one wave of CTAs is in flight (weight streaming);
+// large token counts use 256-token tiles when they alone fill half the GPU,
+// else 128-token tiles.
+void gemm_plan(int M, int N, int kblocks, int sm_count, int* bn_out, int* split_out) {
+  int bn;
+  if (M <= 16) bn = 16;
+  else if (M <= 32) bn = 32;
+  else if (M <= 64) bn = 64;
+  else if (M <= 128) bn = 128;
+  else bn = ((N / 128) * ((M + 255) / 256) >= sm_count / 2) ? 256 : 128;
+  const int tiles = (N / 128) * ((M + bn - 1) / bn);
+  *bn_out = bn;
+  *split_out = gemm_split(tiles, kblocks, sm_count, 8);
+}
 
 int gemm_token_tile(int M) {
   if (M <= 16) return 16;

@@ -8,6 +8,7 @@
 namespace laya {
 
 int gemm_token_tile(int M);
+void gemm_plan(int M, int N, int kblocks, int sm_count, int* bn, int* split);
 int gemm_k_elems(int kind);
 int gemm_split(int tiles, int kblocks, int sm_count, int max_split);
 cudaError_t launch_gemm(int kind, const CUtensorMap& wmap, const CUtensorMap& xmap, const GemmParams& p, int bn,
