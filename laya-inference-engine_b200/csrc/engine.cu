@@ -15,6 +15,7 @@
 #include <cmath>
 #include <cstdarg>
 #include <cstdio>
+#include <algorithm>
 #include <cstring>
 #include <functional>
 #include <map>
@@ -102,8 +103,10 @@ CUtensorMap make_map(const void* ptr, int rows, int cols, int esize, int box_row
 // One projection weight as the GEMM consumes it.
 struct Proj {
   int N = 0, K = 0, kind = kKindBf16;
-  const void* w = nullptr;           // bf16 [N][K] or e4m3 [N][K]
+  const void* w = nullptr;           // bf16 [N][K], e4m3 [N][K] or packed e2m1 [N][K/2]
   const float* w_scale = nullptr;    // fp8 per-row scales
+  const uint8_t* wsf = nullptr;      // nvfp4 scale blocks
+  float w_tensor_scale = 1.f;        // nvfp4 per-tensor outer scale
   const __nv_bfloat16* bias = nullptr;
   CUtensorMap map;
 };
@@ -177,6 +180,10 @@ struct laya_b200_engine {
   float* hsel = nullptr;
   __nv_bfloat16 *asel = nullptr, *nsel = nullptr, *fsel = nullptr, *msc = nullptr, *zsc = nullptr;
   float *gcos = nullptr, *gsin = nullptr, *lcos = nullptr, *lsin = nullptr;
+  uint8_t* x4 = nullptr;            // nvfp4 activation values [T][max(d,I)/2]
+  uint8_t* x4sf = nullptr;          // nvfp4 activation scale blocks
+  float* x4o = nullptr;             // nvfp4 per-row outer scales [T]
+  int x4_col_blocks = 0;
   float* a1 = nullptr;              // tail scratch [max_batch][act_hidden]
   unsigned int* arrivals = nullptr; // tail arrival counters [max_batch]
   // device inputs / outputs (int32 staging layout)
@@ -327,6 +334,46 @@ struct Fwd {
     count(launch_gemm(w.kind, w.map, xmap, p, bn, split, st, pdl()), "gemm launch");
   }
 
+  // NVFP4 projection: quantise the bf16 operand per row (scale blocks laid
+  // out for the GEMM's token tile), then the block-scaled GEMM.
+  void gemm_nv4(const Proj& w, const __nv_bfloat16* x, int M, int epi, __nv_bfloat16* out, int ldo, float* resid,
+                int ldr) {
+    const int kb = (w.K + 255) / 256;
+    int bn = 0, split = 1;
+    gemm_plan(M, w.N, kb, e->sm_count, &bn, &split);
+    if (bn > 128) {
+      bn = 128;
+      const int tiles = (w.N / 128) * ((M + bn - 1) / bn);
+      split = gemm_split(tiles, kb, e->sm_count, 8);
+    }
+    if (on(kCatRows)) {
+      QuantParams q{};
+      q.rows = M;
+      q.k = w.K;
+      q.src = x;
+      q.q = e->x4;
+      q.scale = e->x4o;
+      q.sf = e->x4sf;
+      count(launch_quant_nvfp4(q, bn, 4 * kb, st, pdl()), "nvfp4 quant launch");
+    }
+    if (!on(kCatGemm)) return;
+    CUtensorMap xmap = make_map(e->x4, M, w.K / 2, 1, bn);
+    GemmParams p{};
+    p.M = M;
+    p.N = w.N;
+    p.K = w.K;
+    p.kblocks = kb;
+    p.epilogue = epi;
+    p.out = out;
+    p.ldo = ldo;
+    p.resid = resid;
+    p.ldr = ldr;
+    p.a_scale = e->x4o;
+    p.w_tensor_scale = w.w_tensor_scale;
+    p.status = e->status_dev;
+    count(launch_gemm_nvfp4(w.map, xmap, w.wsf, e->x4sf, kb, p, bn, split, st, pdl()), "nvfp4 gemm launch");
+  }
+
   void norm(NormParams p) {
     if (!on(kCatRows)) return;
     p.eps = e->cfg.norm_eps;
@@ -345,6 +392,7 @@ struct Fwd {
     const int b = sh.b, s = sh.s, k = sh.k, d = c.hidden, I = c.intermediate, F = c.head_ff;
     const int T = b * s, R = b * (1 + k), BK = b * k;
     const bool fp8 = E.precision == LAYA_B200_FP8;
+    const bool nv4 = E.precision == LAYA_B200_NVFP4;
     const IoLayout L = io_layout(sh);
     const int32_t* in = E.d_in;
     const int* ids = in + L.ids;
@@ -389,7 +437,10 @@ struct Fwd {
         }
         norm(p);
       }
-      gemm(E.wqkv[i], fp8 ? (const void*)E.n8 : (const void*)E.n, E.n8s, T, kEpiStore, E.qkv, 3 * d, nullptr, 0);
+      if (nv4)
+        gemm_nv4(E.wqkv[i], E.n, T, kEpiStore, E.qkv, 3 * d, nullptr, 0);
+      else
+        gemm(E.wqkv[i], fp8 ? (const void*)E.n8 : (const void*)E.n, E.n8s, T, kEpiStore, E.qkv, 3 * d, nullptr, 0);
       const bool glob = (i % c.global_every) == 0;
       {
         AttnParams a{};
@@ -415,7 +466,10 @@ struct Fwd {
         q.scale = E.a8s;
         count(launch_quant_fp8(q, st, pdl()), "quant launch");
       }
-      gemm(E.wo[i], fp8 ? (const void*)E.a8 : (const void*)E.attn, E.a8s, T, kEpiResidual, nullptr, 0, E.h, d);
+      if (nv4)
+        gemm_nv4(E.wo[i], E.attn, T, kEpiResidual, nullptr, 0, E.h, d);
+      else
+        gemm(E.wo[i], fp8 ? (const void*)E.a8 : (const void*)E.attn, E.a8s, T, kEpiResidual, nullptr, 0, E.h, d);
       {
         NormParams p{};
         p.rows = T;
@@ -430,7 +484,10 @@ struct Fwd {
         }
         norm(p);
       }
-      gemm(E.wi[i], fp8 ? (const void*)E.n8 : (const void*)E.n, E.n8s, T, kEpiGeglu, E.g, I, nullptr, 0);
+      if (nv4)
+        gemm_nv4(E.wi[i], E.n, T, kEpiGeglu, E.g, I, nullptr, 0);
+      else
+        gemm(E.wi[i], fp8 ? (const void*)E.n8 : (const void*)E.n, E.n8s, T, kEpiGeglu, E.g, I, nullptr, 0);
       if (fp8 && on(kCatRows)) {
         QuantParams q{};
         q.rows = T;
@@ -440,7 +497,10 @@ struct Fwd {
         q.scale = E.g8s;
         count(launch_quant_fp8(q, st, pdl()), "quant launch");
       }
-      gemm(E.wo2[i], fp8 ? (const void*)E.g8 : (const void*)E.g, E.g8s, T, kEpiResidual, nullptr, 0, E.h, d);
+      if (nv4)
+        gemm_nv4(E.wo2[i], E.g, T, kEpiResidual, nullptr, 0, E.h, d);
+      else
+        gemm(E.wo2[i], fp8 ? (const void*)E.g8 : (const void*)E.g, E.g8s, T, kEpiResidual, nullptr, 0, E.h, d);
     }
     // final_norm(h + pending) + type_emb(qtype) (model.py:102-104), fused with
     // the first head layer's norm1 (model.py:59).
@@ -568,10 +628,13 @@ Proj make_proj(laya_b200_engine* e, const std::string& wname, const std::string&
   if (kind == kKindBf16) {
     p.w = e->warena + pi.offset;
     p.map = make_map(p.w, p.N, p.K, 2, 128);
-  } else {
+  } else if (kind == kKindFp8) {
     p.w = qweights;
     p.w_scale = qscale;
     p.map = make_map(p.w, p.N, p.K, 1, 128);
+  } else {  // nvfp4: packed e2m1 [N][K/2]
+    p.w = qweights;
+    p.map = make_map(p.w, p.N, p.K / 2, 1, 128);
   }
   return p;
 }
@@ -675,6 +738,7 @@ int laya_b200_create(int device, const laya_b200_config* cfg, laya_b200_engine**
     const size_t R = (size_t)c.max_batch * (1 + c.max_options);
     const size_t BK = (size_t)c.max_batch * c.max_options;
     e->max_tokens = (int)T;
+    e->x4_col_blocks = 4 * ((std::max(d, I) + 255) / 256);
     const size_t gw = (size_t)(I > F ? I : F);
     std::vector<std::pair<void**, size_t>> bufs = {
         {(void**)&e->h, T * d * 4},         {(void**)&e->n, T * d * 2},
@@ -689,6 +753,9 @@ int laya_b200_create(int device, const laya_b200_config* cfg, laya_b200_engine**
         {(void**)&e->gsin, (size_t)c.max_len * 64 * 4}, {(void**)&e->lcos, (size_t)c.max_len * 64 * 4},
         {(void**)&e->lsin, (size_t)c.max_len * 64 * 4},
         {(void**)&e->a1, (size_t)c.max_batch * c.act_hidden * 4},
+        {(void**)&e->x4, T * (size_t)(d > I ? d : I) / 2},
+        {(void**)&e->x4sf, ((T + 15) / 16) * (size_t)(4 * ((std::max(d, I) + 255) / 256)) * 512},
+        {(void**)&e->x4o, T * 4},
         {(void**)&e->arrivals, (size_t)c.max_batch * 4},
     };
     size_t aoff = 0;
@@ -768,10 +835,11 @@ int laya_b200_finalize(laya_b200_engine* e, int precision) {
     if (e->finalized) fail("already finalized");
     for (auto& kv : e->params)
       if (!kv.second.uploaded) fail("parameter %s was not uploaded", kv.first.c_str());
-    if (precision != LAYA_B200_BF16 && precision != LAYA_B200_FP8)
-      fail("precision %d is not available in this build", precision);
+    if (precision != LAYA_B200_BF16 && precision != LAYA_B200_FP8 && precision != LAYA_B200_NVFP4)
+      fail("unknown precision %d", precision);
     const laya_b200_config& c = e->cfg;
-    const int kind = precision == LAYA_B200_FP8 ? kKindFp8 : kKindBf16;
+    const int kind = precision == LAYA_B200_FP8 ? kKindFp8 : precision == LAYA_B200_NVFP4 ? kKindNvfp4 : kKindBf16;
+    if (kind == kKindNvfp4 && (c.hidden % 16 || c.intermediate % 16)) fail("NVFP4 needs K divisible by 16");
     std::vector<std::pair<std::string, size_t>> qoff;  // weight name -> offset of e4m3 bytes, scales follow
     if (kind == kKindFp8) {
       size_t off = 0;
@@ -795,8 +863,54 @@ int laya_b200_finalize(laya_b200_engine* e, int precision) {
       }
       ck(cudaStreamSynchronize(e->stream), "fp8 packer");
     }
+    // NVFP4: per weight [e2m1 N*K/2 | scale blocks (N/128) x 4*ceil(K/256) x 512 | tensor scale]
+    struct Nv4 {
+      std::string name;
+      size_t q, sf, ts;
+      int col_blocks;
+    };
+    std::vector<Nv4> nv4;
+    if (kind == kKindNvfp4) {
+      size_t off = 0;
+      for (int i = 0; i < c.layers; ++i)
+        for (const char* nm : {"wqkv", "wo", "wi", "wo2"}) {
+          const std::string name = "enc." + std::to_string(i) + "." + nm;
+          const ParamInfo& pi = e->params.at(name);
+          Nv4 w{name, off, 0, 0, 4 * ((pi.cols + 255) / 256)};
+          off = align_up(off + pi.elems / 2, 256);
+          w.sf = off;
+          off = align_up(off + (size_t)(pi.rows / 128) * w.col_blocks * 512, 256);
+          w.ts = off;
+          off = align_up(off + 4, 256);
+          nv4.push_back(w);
+        }
+      const size_t scratch = off;
+      off = align_up(off + 4, 256);
+      e->qarena_bytes = off;
+      ck(cudaMalloc(&e->qarena, off), "packed weight arena");
+      ck(cudaMemset(e->qarena, 0, off), "packed weight arena");  // zero scale padding
+      for (auto& w : nv4) {
+        const ParamInfo& pi = e->params.at(w.name);
+        ck(launch_nvfp4_pack_weight(reinterpret_cast<const __nv_bfloat16*>(e->warena + pi.offset), pi.rows, pi.cols,
+                                    reinterpret_cast<unsigned int*>(e->qarena + scratch), e->qarena + w.q,
+                                    e->qarena + w.sf, w.col_blocks, reinterpret_cast<float*>(e->qarena + w.ts),
+                                    e->stream),
+           "nvfp4 packer");
+      }
+      ck(cudaStreamSynchronize(e->stream), "nvfp4 packer");
+    }
     auto enc_proj = [&](const std::string& name) {
       if (kind == kKindBf16) return make_proj(e, name, "", kKindBf16, nullptr, nullptr);
+      if (kind == kKindNvfp4) {
+        for (auto& w : nv4)
+          if (w.name == name) {
+            Proj p = make_proj(e, name, "", kKindNvfp4, e->qarena + w.q, nullptr);
+            p.wsf = e->qarena + w.sf;
+            ck(cudaMemcpy(&p.w_tensor_scale, e->qarena + w.ts, 4, cudaMemcpyDeviceToHost), "tensor scale");
+            return p;
+          }
+        fail("no packed weights for %s", name.c_str());
+      }
       for (auto& q : qoff)
         if (q.first == name) {
           const ParamInfo& pi = e->params.at(name);

@@ -13,9 +13,13 @@ int gemm_k_elems(int kind);
 int gemm_split(int tiles, int kblocks, int sm_count, int max_split);
 cudaError_t launch_gemm(int kind, const CUtensorMap& wmap, const CUtensorMap& xmap, const GemmParams& p, int bn,
                         int split, cudaStream_t stream, bool pdl);
-cudaError_t launch_gemm_nvfp4(const CUtensorMap& wmap, const CUtensorMap& xmap, const CUtensorMap& wsf,
-                              const CUtensorMap& xsf, const GemmParams& p, int bn, int split, cudaStream_t stream,
-                              bool pdl);
+cudaError_t launch_gemm_nvfp4(const CUtensorMap& wmap, const CUtensorMap& xmap, const uint8_t* wsf,
+                              const uint8_t* xsf, int sf_kbs, const GemmParams& p, int bn, int split,
+                              cudaStream_t stream, bool pdl);
+cudaError_t launch_nvfp4_pack_weight(const __nv_bfloat16* w, int rows, int k, unsigned int* amax_scratch, uint8_t* q,
+                                     uint8_t* sf, int col_blocks, float* tensor_scale, cudaStream_t stream);
+cudaError_t launch_quant_nvfp4(const QuantParams& p, int rows_per_block, int col_blocks, cudaStream_t stream,
+                               bool pdl);
 cudaError_t launch_attention(const AttnParams& p, int batch, int heads, cudaStream_t stream, bool pdl);
 cudaError_t launch_norm(const NormParams& p, cudaStream_t stream, bool pdl);
 cudaError_t launch_quant_fp8(const QuantParams& p, cudaStream_t stream, bool pdl);

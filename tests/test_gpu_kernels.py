@@ -115,3 +115,37 @@ def test_local_window_and_head_select():
             assert np.isfinite(logits).all() and np.isfinite(act).all()
     finally:
         nf.close()
+
+
+@pytest.mark.parametrize("precision", ["nvfp4", "fp8"])
+def test_low_precision_qkv_stage_matches_oracle(precision):
+    """Layer-0 QKV projection under FP8 / NVFP4 against the oracle's quantised
+    linear on the same bf16 input (fp32 accumulation order differs, so a few
+    outputs differ by one bf16 ulp)."""
+    from laya_b200.engine import NativeForward
+    cfg = MICRO
+    w = seeded_weights(cfg, seed=3)
+    nf = NativeForward(0, cfg, w, precision, max_batch=4, max_options=8)
+    try:
+        b, s, k = 2, 192, 4
+        items = synthetic_items([192, 100], ["choice", "noul"], seed=11, vocab=cfg.vocab)
+        inp = pack(items, b, s, k, cfg.pad_token_id)
+        slot = nf.capture(b, s, k, False)
+        logits, act = nf.run(slot, inp)
+        T, d = b * s, cfg.hidden
+        qkv = bf16_of(nf.read_buffer("qkv", (T, 3 * d), np.uint16))
+    finally:
+        nf.close()
+    wf = {kk: torch.from_numpy(v) for kk, v in as_float32(w).items()}
+    ids = torch.from_numpy(inp["input_ids"]).reshape(-1)
+    n0 = O.bf16(O.layer_norm(wf["embed.tok"][ids], wf["embed.norm.w"], None, cfg.norm_eps))
+    ref = O.encoder_linear(n0, wf["enc.0.wqkv"], precision, {}, "wqkv")
+    err = float((qkv - ref).abs().max())
+    rel = float(((qkv - ref).abs() / ref.abs().clamp_min(1e-2)).median())
+    print(f"{precision} qkv: max-abs {err:.3e}, median rel {rel:.2e}")
+    assert err < 3e-2, err
+    orc = O.Oracle(w, cfg, precision)
+    ol, oa = orc.forward(**inp)
+    mm = inp["marker_mask"]
+    tol = {"fp8": 6e-2, "nvfp4": 1.5e-1}[precision]
+    assert np.abs(logits[mm] - ol[mm]).max() <= tol and np.abs(act - oa).max() <= tol

@@ -129,3 +129,18 @@ def test_fp8_matches_fp8_oracle(name, lengths, s, k):
     bl, _ = oracle_for(name, "bf16").forward(**inp)
     agree = O.decision_agreement(bl, logits, inp["marker_mask"])
     print(f"fp8 decision agreement with the bf16 oracle: {agree:.3f}")
+
+
+def test_nvfp4_long_question_matches_nvfp4_oracle():
+    """NVFP4, one question at the model maximum (s=512):
+    10 global layers and 18 radius-64 local layers."""
+    name, s = "laya", 512
+    nf = engine_for(name, "nvfp4")
+    items = synthetic_items([512], ["choice"], seed=40, vocab=CONFIGS[name].vocab)
+    inp = pack(items, 1, s, 4, CONFIGS[name].pad_token_id)
+    slot = nf.capture(1, s, 4, True)
+    logits, act = nf.run(slot, inp)
+    ol, oa = oracle_for(name, "nvfp4").forward(**inp)
+    compare(logits, act, ol, oa, inp["marker_mask"], TOL["nvfp4"], "nvfp4 C3 vs nvfp4 oracle")
+    bl, _ = oracle_for(name, "bf16").forward(**inp)
+    print(f"nvfp4 decision agreement with the bf16 oracle: {O.decision_agreement(bl, logits, inp['marker_mask']):.3f}")
