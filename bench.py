@@ -51,6 +51,9 @@ def parse():
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--precision", default="bf16", choices=["bf16", "fp8"])
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
+    ap.add_argument("--workload", default="c1", choices=["c1", "c2", "c3", "c4"],
+                    help="c1 (default, the contract line): b=1 s=64 noul; c2: FP8 16x96; c3: NVFP4 1x512; "
+                         "c4: FP8 64 questions s~U[32,512] bucketed by 32, sharded over ranks")
     return ap.parse_args()
 
 
@@ -223,10 +226,125 @@ def run_reference(args):
     return 0
 
 
+def encoder_flops(cfg, items):
+    """Algorithmic FLOPs of one forward over the valid tokens of `items`:
+    encoder projections 2*params*tokens, attention 4*d*sum(visible keys),
+    head layers (last one on 1+k rows) and the scorer."""
+    d, I, F, H = cfg.hidden, cfg.intermediate, cfg.head_ff, cfg.layers
+    proj = 3 * d * d + d * d + 2 * I * d + d * I
+    fl = 0
+    for it in items:
+        n, k = len(it["ids"]), len(it["markers"])
+        fl += 2 * proj * n * H
+        for layer in range(H):
+            if cfg.is_global(layer):
+                keys = n * n
+            else:
+                w = cfg.window
+                keys = sum(min(n, i + w + 1) - max(0, i - w) for i in range(n))
+            fl += 4 * d * keys
+        fl += 2 * (3 * d * d + d * d + 2 * F * d) * n                     # head layer 0
+        fl += 2 * (2 * d * d) * n + 2 * (d * d + d * d + 2 * F * d) * (1 + k) + 4 * d * n * (1 + k)  # last layer
+        fl += 2 * d * d * k
+    return fl
+
+
+def run_batched(args):
+    """C2 / C3 / C4: batched requests through the public engine API."""
+    rank, world, local, dist = dist_setup(args.gpus)
+    import torch
+    from laya_b200.config import LAYA
+    from laya_b200.engine import B200Engine, request_from_items
+    from laya_b200.workload import synthetic_items, mixed_kinds
+    from laya_b200.dispatcher import c4_step, shard_for_rank, group_by_bucket
+    cfg = LAYA
+    w = args.workload
+    if w == "c2":
+        precision, buckets = "fp8", (96,)
+        steps_items = [synthetic_items([96] * 16, mixed_kinds(16, s), seed=100 + s, vocab=cfg.vocab) for s in range(2)]
+    elif w == "c3":
+        precision, buckets = "nvfp4", (512,)
+        steps_items = [synthetic_items([512], ["choice"], seed=200 + s, vocab=cfg.vocab) for s in range(2)]
+    else:
+        precision, buckets = "fp8", tuple(range(32, 513, 32))
+        steps_items = [c4_step(300 + s, cfg.vocab) for s in range(4)]
+    eng = B200Engine(config=cfg, device=local, precision=precision, max_questions=64, max_options=4,
+                     max_graphs=512, sequence_buckets=buckets)
+    plans = []
+    for items in steps_items:
+        mine = shard_for_rank(items, world, rank, buckets) if world > 1 else list(range(len(items)))
+        groups = group_by_bucket(items, mine, buckets, 64)
+        plans.append([request_from_items([items[i] for i in idx]) for _, idx in groups])
+    for plan in plans * max(1, args.warmup // len(plans)):     # captures every shape, then warm
+        for req in plan:
+            eng.run_prepared(req)
+
+    def barrier():
+        if dist:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    def max_over_ranks(x):
+        if not dist:
+            return x
+        t = torch.tensor([x], dtype=torch.float64, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    # device time per step: the step's graphs replayed back to back with inputs resident
+    dev_ms = []
+    for plan in plans:
+        t = 0.0
+        for req in plan:
+            eng.run_prepared(req)
+            slot = eng.graphs[eng._graph_key(req)]
+            t += float(np.mean(eng.native.replay_device(slot, 5)))
+        dev_ms.append(t)
+    with ClockSampler(local) as clocks:
+        barrier()
+        t0 = time.perf_counter()
+        for k in range(args.steps):
+            for req in plans[k % len(plans)]:
+                eng.run_prepared(req)
+        wall = max_over_ranks(time.perf_counter() - t0)
+        barrier()
+    questions = sum(len(it) for it in steps_items) / len(steps_items)
+    dev_step = max_over_ranks(float(np.mean(dev_ms)))
+    value = questions / (dev_step / 1000.0)
+    e2e = args.steps * questions / wall
+    flops = float(np.mean([encoder_flops(cfg, items) for items in steps_items]))
+    d = json.loads((ROOT / "MEASURED_PEAKS.json").read_text()) if (ROOT / "MEASURED_PEAKS.json").exists() else {}
+    bf16_peak = float(d.get("bf16_tflops", 1590.0))
+    peak = 2 * bf16_peak if precision == "fp8" else 4 * bf16_peak if precision == "nvfp4" else bf16_peak
+    achieved = flops / (dev_step / 1000.0) / 1e12 / world
+    if rank == 0:
+        cs = clocks.summary()
+        line = {"metric": "decisions/s", "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+                "warmup": args.warmup, "ms_per_step": dev_step, "higher_is_better": True, "scaling": "weak" if w != "c4" else "strong",
+                "vs_baseline": None, "dtype": {"fp8": "e4m3", "nvfp4": "e2m1"}[precision], "data": "synthetic",
+                "config": {"workload": w, "precision": precision, "questions_per_step": questions,
+                           "buckets": list(buckets) if len(buckets) < 5 else "multiples of 32 up to 512",
+                           "parallelism": f"request-parallel x{world}"},
+                "e2e": {"value": e2e, "unit": UNIT, "path": "B200Engine.run_prepared per bucket group"},
+                "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+                             "frac": achieved / peak, "flops_per_step": flops,
+                             "peak_source": f"{'2x' if precision == 'fp8' else '4x' if precision == 'nvfp4' else '1x'} "
+                                            "measured cuBLAS bf16 (MEASURED_PEAKS.json)"},
+                "clocks": cs}
+        print(json.dumps(line), flush=True)
+    eng.close()
+    if dist:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
 def main():
     args = parse()
     if args.impl == "reference":
         return run_reference(args)
+    if args.workload != "c1":
+        return run_batched(args)
     if args.warmup < 3:
         raise SystemExit("--warmup must be at least 3")
     rank, world, local, dist = dist_setup(args.gpus)
