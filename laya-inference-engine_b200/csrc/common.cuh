@@ -53,6 +53,10 @@ DEVI void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
                : "memory");
 }
 
+DEVI void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.release.cta.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
 DEVI bool mbar_try(uint32_t addr, uint32_t parity) {
   uint32_t ok;
   asm volatile(
