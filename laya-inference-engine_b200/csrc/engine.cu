@@ -100,6 +100,23 @@ CUtensorMap make_map(const void* ptr, int rows, int cols, int esize, int box_row
   return m;
 }
 
+// Plain (unswizzled) 2D map for the TMA epilogue: a [rows][ld] row-major
+// buffer of `esize`-byte elements, box = box_cols x box_rows.  Returns false
+// when the driver rejects the geometry (the caller then uses the register
+// epilogue).
+bool make_plain_map(CUtensorMap* m, const void* ptr, int rows, int ld, int esize, int box_cols, int box_rows) {
+  EncodeTiledFn enc = get_encode_fn();
+  if (!enc) return false;
+  const CUtensorMapDataType dt = esize == 2 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
+  cuuint64_t dims[2] = {(cuuint64_t)ld, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)ld * esize};
+  cuuint32_t box[2] = {(cuuint32_t)box_cols, (cuuint32_t)box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  return enc(m, dt, 2, const_cast<void*>(ptr), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+             CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) ==
+         CUDA_SUCCESS;
+}
+
 // One projection weight as the GEMM consumes it.
 struct Proj {
   int N = 0, K = 0, kind = kKindBf16;
@@ -331,7 +348,10 @@ struct Fwd {
     p.a_scale = x_scale;
     p.w_scale = w.w_scale;
     p.status = e->status_dev;
-    count(launch_gemm(w.kind, w.map, xmap, p, bn, split, st, pdl()), "gemm launch");
+    CUtensorMap omap;
+    memset(&omap, 0, sizeof(omap));
+    if (split == 1 && bn >= 128) p.tma_epilogue = output_map(&omap, p, bn);
+    count(launch_gemm(w.kind, w.map, xmap, omap, p, bn, split, st, pdl()), "gemm launch");
   }
 
   // NVFP4 projection: quantise the bf16 operand per row (scale blocks laid
@@ -371,7 +391,17 @@ struct Fwd {
     p.a_scale = e->x4o;
     p.w_tensor_scale = w.w_tensor_scale;
     p.status = e->status_dev;
-    count(launch_gemm_nvfp4(w.map, xmap, w.wsf, e->x4sf, kb, p, bn, split, st, pdl()), "nvfp4 gemm launch");
+    CUtensorMap omap;
+    memset(&omap, 0, sizeof(omap));
+    if (split == 1 && bn >= 128) p.tma_epilogue = output_map(&omap, p, bn);
+    count(launch_gemm_nvfp4(w.map, xmap, omap, w.wsf, e->x4sf, kb, p, bn, split, st, pdl()), "nvfp4 gemm launch");
+  }
+
+  // Output tensor map of the TMA epilogue (unsplit tiles).
+  static int output_map(CUtensorMap* m, const GemmParams& p, int bn) {
+    if (p.epilogue == kEpiResidual) return make_plain_map(m, p.resid, p.M, p.ldr, 4, 128, bn) ? 1 : 0;
+    const int cols = p.epilogue == kEpiGeglu ? 64 : 128;
+    return make_plain_map(m, p.out, p.M, p.ldo, 2, cols, bn) ? 1 : 0;
   }
 
   void norm(NormParams p) {

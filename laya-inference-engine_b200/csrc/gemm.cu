@@ -45,9 +45,9 @@ struct GemmCfg {
 };
 
 template <int BN, int KIND, int STAGES>
-__global__ void __launch_bounds__(128, 1)
+__global__ void __launch_bounds__(BN >= 128 ? 256 : 128, BN == 128 ? 2 : 1)
     gemm_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ CUtensorMap xmap,
-                const GemmParams p) {
+                const __grid_constant__ CUtensorMap omap, const GemmParams p) {
   using C = GemmCfg<BN, KIND, STAGES>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -56,7 +56,8 @@ __global__ void __launch_bounds__(128, 1)
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::MAIN_BYTES);
   uint64_t* empty = full + STAGES;
   uint64_t* done = empty + STAGES;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
+  uint64_t* rbar = done + 1;  // residual tile load of the TMA epilogue
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(rbar + 1);
   uint32_t* failed = tmem_slot + 1;
 
   const int tid = threadIdx.x, warp = tid >> 5;
@@ -74,6 +75,7 @@ __global__ void __launch_bounds__(128, 1)
       mbar_init(&empty[s], 1);
     }
     mbar_init(done, 1);
+    mbar_init(rbar, 1);
     *failed = 0;
     fence_mbar_init();
     prefetch_tensormap(&wmap);
@@ -145,7 +147,10 @@ __global__ void __launch_bounds__(128, 1)
     atomicExch(failed, 1u);
   }
   tc_fence_after();
-  tile_epilogue<BN, KIND>(p, tmem, reinterpret_cast<float*>(smem), tile_n, tile_m, split, rank);
+  if (split == 1 && p.tma_epilogue && BN >= 128)
+    tile_epilogue_wide<BN, KIND, 256>(p, &omap, tmem, smem, tile_n, tile_m);
+  else
+    tile_epilogue<BN, KIND>(p, tmem, reinterpret_cast<float*>(smem), tile_n, tile_m, split, rank);
 
   // ---- teardown: drain copies still in flight after a failure, free TMEM
   if (tid == 0 && *failed) {
@@ -162,7 +167,8 @@ __global__ void __launch_bounds__(128, 1)
 namespace {
 
 template <int BN, int KIND, int STAGES>
-cudaError_t launch_one(const CUtensorMap& wmap, const CUtensorMap& xmap, const GemmParams& p, int tiles_n,
+cudaError_t launch_one(const CUtensorMap& wmap, const CUtensorMap& xmap, const CUtensorMap& omap, const GemmParams& p,
+                       int tiles_n,
                        int tiles_m, int split, cudaStream_t stream, bool pdl) {
   using C = GemmCfg<BN, KIND, STAGES>;
   auto kern = gemm_kernel<BN, KIND, STAGES>;
@@ -183,7 +189,7 @@ cudaError_t launch_one(const CUtensorMap& wmap, const CUtensorMap& xmap, const G
   }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(tiles_n, tiles_m, split);
-  cfg.blockDim = dim3(128, 1, 1);
+  cfg.blockDim = dim3(BN >= 128 ? 256 : 128, 1, 1);
   cfg.dynamicSmemBytes = C::SMEM;
   cfg.stream = stream;
   cudaLaunchAttribute attrs[2];
@@ -202,18 +208,19 @@ cudaError_t launch_one(const CUtensorMap& wmap, const CUtensorMap& xmap, const G
   }
   cfg.attrs = attrs;
   cfg.numAttrs = na;
-  return cudaLaunchKernelEx(&cfg, kern, wmap, xmap, p);
+  return cudaLaunchKernelEx(&cfg, kern, wmap, xmap, omap, p);
 }
 
 template <int KIND>
-cudaError_t dispatch_bn(int bn, const CUtensorMap& wmap, const CUtensorMap& xmap, const GemmParams& p, int tn,
+cudaError_t dispatch_bn(int bn, const CUtensorMap& wmap, const CUtensorMap& xmap, const CUtensorMap& omap,
+                        const GemmParams& p, int tn,
                         int tm, int split, cudaStream_t st, bool pdl) {
   switch (bn) {
-    case 16: return launch_one<16, KIND, 4>(wmap, xmap, p, tn, tm, split, st, pdl);
-    case 32: return launch_one<32, KIND, 4>(wmap, xmap, p, tn, tm, split, st, pdl);
-    case 64: return launch_one<64, KIND, 4>(wmap, xmap, p, tn, tm, split, st, pdl);
-    case 128: return launch_one<128, KIND, 3>(wmap, xmap, p, tn, tm, split, st, pdl);
-    case 256: return launch_one<256, KIND, 4>(wmap, xmap, p, tn, tm, split, st, pdl);
+    case 16: return launch_one<16, KIND, 4>(wmap, xmap, omap, p, tn, tm, split, st, pdl);
+    case 32: return launch_one<32, KIND, 4>(wmap, xmap, omap, p, tn, tm, split, st, pdl);
+    case 64: return launch_one<64, KIND, 4>(wmap, xmap, omap, p, tn, tm, split, st, pdl);
+    case 128: return launch_one<128, KIND, 3>(wmap, xmap, omap, p, tn, tm, split, st, pdl);
+    case 256: return launch_one<256, KIND, 4>(wmap, xmap, omap, p, tn, tm, split, st, pdl);
   }
   return cudaErrorInvalidValue;
 }
@@ -259,13 +266,13 @@ int gemm_split(int tiles, int kblocks, int sm_count, int max_split) {
   return s;
 }
 
-cudaError_t launch_gemm(int kind, const CUtensorMap& wmap, const CUtensorMap& xmap, const GemmParams& p, int bn,
-                        int split, cudaStream_t stream, bool pdl) {
+cudaError_t launch_gemm(int kind, const CUtensorMap& wmap, const CUtensorMap& xmap, const CUtensorMap& omap,
+                        const GemmParams& p, int bn, int split, cudaStream_t stream, bool pdl) {
   const int tiles_n = p.N / 128;
   const int tiles_m = (p.M + bn - 1) / bn;
   if (p.N % 128 || split < 1 || split > 16 || split > p.kblocks) return cudaErrorInvalidValue;
-  if (kind == kKindBf16) return dispatch_bn<kKindBf16>(bn, wmap, xmap, p, tiles_n, tiles_m, split, stream, pdl);
-  if (kind == kKindFp8) return dispatch_bn<kKindFp8>(bn, wmap, xmap, p, tiles_n, tiles_m, split, stream, pdl);
+  if (kind == kKindBf16) return dispatch_bn<kKindBf16>(bn, wmap, xmap, omap, p, tiles_n, tiles_m, split, stream, pdl);
+  if (kind == kKindFp8) return dispatch_bn<kKindFp8>(bn, wmap, xmap, omap, p, tiles_n, tiles_m, split, stream, pdl);
   return cudaErrorInvalidValue;
 }
 

@@ -92,7 +92,9 @@ DEVI void tile_epilogue(const GemmParams& p, uint32_t tmem, float* part, int til
                         int rank) {
   const int tid = threadIdx.x, warp = tid >> 5;
   const uint32_t lane_addr = tmem + ((uint32_t)(warp * 32) << 16);
-  if (BN >= 32) {
+  if (tid >= 128) {
+    // CTAs of more than 128 threads: only warps 0-3 own TMEM lanes
+  } else if (BN >= 32) {
 #pragma unroll 1
     for (int c = 0; c < BN; c += 32) {
       uint32_t r[32];
@@ -120,7 +122,7 @@ DEVI void tile_epilogue(const GemmParams& p, uint32_t tmem, float* part, int til
   // 16-byte DSMEM loads issued back to back.
   const int t0 = rank * BN / split, t1 = (rank + 1) * BN / split, nt = t1 - t0;
   const uint32_t part_addr = smem_u32(part);
-  for (int item = tid; item < nt * 16; item += 128) {
+  for (int item = tid; tid < 128 && item < nt * 16; item += 128) {
     const int tl = t0 + (item >> 4);
     const int q4 = (item & 15) * 4;
     const int m = tile_m * BN + tl;
@@ -155,6 +157,159 @@ DEVI void tile_epilogue(const GemmParams& p, uint32_t tmem, float* part, int til
   }
   if (split > 1) cluster_sync_all();
 
+}
+
+// Epilogue of an unsplit tile with THREADS (256) threads.  Warps 0-3 (the
+// four TMEM lane quarters) dump the raw fp32 accumulator into shared memory
+// as P[token][128 weight rows]; then every thread takes (token, 4 rows)
+// items, applies the precision's scales, bias and activation, and either
+// writes the bf16 result into a shared [token][features] tile that one TMA
+// store copies out (store / ReLU / GELU / GEGLU), or updates the fp32
+// residual in global memory with 16-byte loads issued eight items at a time.
+// Spreading the arithmetic (erf for GELU) over eight warps instead of the
+// four TMEM warps keeps two warps per SM sub-partition busy.
+template <int BN, int KIND, int THREADS>
+DEVI void tile_epilogue_wide(const GemmParams& p, const CUtensorMap* omap, uint32_t tmem, uint8_t* smem, int tile_n,
+                             int tile_m) {
+  const int tid = threadIdx.x, warp = tid >> 5;
+  const int m_base = tile_m * BN;
+  const int ep = p.epilogue;
+  float* P = reinterpret_cast<float*>(smem);
+  __nv_bfloat16* O = reinterpret_cast<__nv_bfloat16*>(smem + BN * 512);
+  float* S = reinterpret_cast<float*>(smem + BN * 512 + BN * 256);
+  if (tid < 128) {
+    const uint32_t lane_addr = tmem + ((uint32_t)(warp * 32) << 16);
+    constexpr int CH = BN >= 32 ? 32 : 16;
+#pragma unroll 1
+    for (int c = 0; c < BN; c += CH) {
+      uint32_t v[32];
+      if (CH == 32) {
+        tmem_ld32(lane_addr + c, v);
+      } else {
+        uint32_t v16[16];
+        tmem_ld16(lane_addr + c, v16);
+#pragma unroll
+        for (int j = 0; j < 16; ++j) v[j] = v16[j];
+      }
+      tmem_wait_ld();
+#pragma unroll
+      for (int j = 0; j < CH; ++j) P[(c + j) * 128 + tid] = __uint_as_float(v[j]);
+    }
+  }
+  if (KIND != kKindBf16)
+    for (int i = tid; i < BN; i += THREADS) S[i] = m_base + i < p.M ? p.a_scale[m_base + i] : 0.f;
+  __syncthreads();
+  const float tsc = KIND == kKindNvfp4 ? p.w_tensor_scale : 1.f;
+  // item = (token, quad): rows 4q..4q+3 (GEGLU: act rows 4q..4q+3 of 64, gate rows +64)
+  const int quads = ep == kEpiGeglu ? 16 : 32;
+  const int items = BN * quads;
+  if (ep == kEpiResidual) {
+    constexpr int BATCH = 8;
+    for (int i0 = tid; i0 < items; i0 += THREADS * BATCH) {
+      float4 res[BATCH];
+#pragma unroll
+      for (int u = 0; u < BATCH; ++u) {
+        const int it = i0 + u * THREADS;
+        const int tok = it >> 5, q = it & 31, m = m_base + tok;
+        if (it < items && m < p.M)
+          res[u] = *reinterpret_cast<const float4*>(p.resid + (size_t)m * p.ldr + tile_n * 128 + 4 * q);
+      }
+#pragma unroll
+      for (int u = 0; u < BATCH; ++u) {
+        const int it = i0 + u * THREADS;
+        const int tok = it >> 5, q = it & 31, m = m_base + tok;
+        if (it >= items || m >= p.M) continue;
+        const int n = tile_n * 128 + 4 * q;
+        float4 a = *reinterpret_cast<const float4*>(P + tok * 128 + 4 * q);
+        float x[4] = {a.x, a.y, a.z, a.w};
+        if (KIND == kKindFp8) {
+          const float4 w = *reinterpret_cast<const float4*>(p.w_scale + n);
+          const float ww[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+          for (int e = 0; e < 4; ++e) x[e] = (x[e] * S[tok]) * ww[e];
+        } else if (KIND == kKindNvfp4) {
+#pragma unroll
+          for (int e = 0; e < 4; ++e) x[e] *= S[tok] * tsc;
+        }
+        if (p.bias) {
+          const uint2 bu = *reinterpret_cast<const uint2*>(p.bias + n);
+          const __nv_bfloat16* bb = reinterpret_cast<const __nv_bfloat16*>(&bu);
+#pragma unroll
+          for (int e = 0; e < 4; ++e) x[e] += __bfloat162float(bb[e]);
+        }
+        float4 r = res[u];
+        r.x += bf16_round(x[0]);
+        r.y += bf16_round(x[1]);
+        r.z += bf16_round(x[2]);
+        r.w += bf16_round(x[3]);
+        *reinterpret_cast<float4*>(p.resid + (size_t)m * p.ldr + n) = r;
+      }
+    }
+    __syncthreads();
+    return;
+  }
+  for (int it = tid; it < items; it += THREADS) {
+    const int tok = it / quads, q = it % quads;
+    const int r0 = 4 * q;
+    float x[4], g[4];
+    {
+      const float4 a = *reinterpret_cast<const float4*>(P + tok * 128 + r0);
+      x[0] = a.x; x[1] = a.y; x[2] = a.z; x[3] = a.w;
+      if (ep == kEpiGeglu) {
+        const float4 b = *reinterpret_cast<const float4*>(P + tok * 128 + 64 + r0);
+        g[0] = b.x; g[1] = b.y; g[2] = b.z; g[3] = b.w;
+      }
+    }
+    const int n = tile_n * 128 + r0;
+    if (KIND == kKindFp8) {
+      const float4 w = *reinterpret_cast<const float4*>(p.w_scale + n);
+      const float ww[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+      for (int e = 0; e < 4; ++e) x[e] = (x[e] * S[tok]) * ww[e];
+      if (ep == kEpiGeglu) {
+        const float4 w2 = *reinterpret_cast<const float4*>(p.w_scale + n + 64);
+        const float wg[4] = {w2.x, w2.y, w2.z, w2.w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) g[e] = (g[e] * S[tok]) * wg[e];
+      }
+    } else if (KIND == kKindNvfp4) {
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        x[e] *= S[tok] * tsc;
+        g[e] *= S[tok] * tsc;
+      }
+    }
+    __nv_bfloat16 o[4];
+    if (ep == kEpiGeglu) {
+#pragma unroll
+      for (int e = 0; e < 4; ++e)
+        o[e] = __float2bfloat16_rn(bf16_round(gelu_erf(bf16_round(x[e]))) * bf16_round(g[e]));
+      *reinterpret_cast<uint2*>(O + tok * 64 + r0) = *reinterpret_cast<uint2*>(o);
+    } else {
+      if (p.bias) {
+        const uint2 bu = *reinterpret_cast<const uint2*>(p.bias + n);
+        const __nv_bfloat16* bb = reinterpret_cast<const __nv_bfloat16*>(&bu);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) x[e] += __bfloat162float(bb[e]);
+      }
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        float y = x[e];
+        if (ep == kEpiRelu) y = fmaxf(y, 0.f);
+        else if (ep == kEpiGelu) y = gelu_erf(bf16_round(y));
+        o[e] = __float2bfloat16_rn(y);
+      }
+      *reinterpret_cast<uint2*>(O + tok * 128 + r0) = *reinterpret_cast<uint2*>(o);
+    }
+  }
+  fence_proxy_async_smem();
+  __syncthreads();
+  if (tid == 0) {
+    tma_store_2d(omap, O, ep == kEpiGeglu ? tile_n * 64 : tile_n * 128, m_base);
+    bulk_commit();
+    bulk_wait_read0();
+  }
+  __syncthreads();
 }
 
 }  // namespace laya

@@ -59,7 +59,7 @@ struct Nvf4Cfg {
   static constexpr int SF_BYTES = 2048;  // four 512-byte scale blocks per operand per k-block
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES + 2 * SF_BYTES;
   static constexpr int PIPE_BYTES = STAGES * STAGE_BYTES;
-  static constexpr int PART_BYTES = BN * 128 * 4;
+  static constexpr int PART_BYTES = BN >= 128 ? BN * 128 * 4 + BN * 128 * 2 + BN * 4 : BN * 128 * 4;
   static constexpr int MAIN_BYTES = PIPE_BYTES > PART_BYTES ? PIPE_BYTES : PART_BYTES;
   static constexpr int SMEM = MAIN_BYTES + 256 + 1024;
   static constexpr int TMEM_NEED = BN + STAGES * 32;
@@ -67,10 +67,10 @@ struct Nvf4Cfg {
 };
 
 template <int BN, int STAGES>
-__global__ void __launch_bounds__(128, 1)
+__global__ void __launch_bounds__(BN >= 128 ? 256 : 128, BN == 128 ? 2 : 1)
     gemm_nvfp4_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ CUtensorMap xmap,
-                      const uint8_t* __restrict__ wsf, const uint8_t* __restrict__ xsf, int sf_kbs,
-                      const GemmParams p) {
+                      const __grid_constant__ CUtensorMap omap, const uint8_t* __restrict__ wsf,
+                      const uint8_t* __restrict__ xsf, int sf_kbs, const GemmParams p) {
   using C = Nvf4Cfg<BN, STAGES>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -81,7 +81,8 @@ __global__ void __launch_bounds__(128, 1)
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::MAIN_BYTES);
   uint64_t* empty = full + STAGES;
   uint64_t* done = empty + STAGES;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
+  uint64_t* rbar = done + 1;  // residual tile load of the TMA epilogue
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(rbar + 1);
   uint32_t* failed = tmem_slot + 1;
 
   const int tid = threadIdx.x, warp = tid >> 5;
@@ -98,6 +99,7 @@ __global__ void __launch_bounds__(128, 1)
       mbar_init(&empty[s], 1);
     }
     mbar_init(done, 1);
+    mbar_init(rbar, 1);
     *failed = 0;
     fence_mbar_init();
     prefetch_tensormap(&wmap);
@@ -178,7 +180,10 @@ __global__ void __launch_bounds__(128, 1)
     atomicExch(failed, 1u);
   }
   tc_fence_after();
-  tile_epilogue<BN, kKindNvfp4>(p, tmem, reinterpret_cast<float*>(smem), tile_n, tile_m, split, rank);
+  if (split == 1 && p.tma_epilogue && BN >= 128)
+    tile_epilogue_wide<BN, kKindNvfp4, 256>(p, &omap, tmem, smem, tile_n, tile_m);
+  else
+    tile_epilogue<BN, kKindNvfp4>(p, tmem, reinterpret_cast<float*>(smem), tile_n, tile_m, split, rank);
 
   if (tid == 0 && *failed) {
     for (int i = (issued > STAGES ? issued - STAGES : 0); i < issued; ++i)
@@ -278,7 +283,8 @@ __global__ void __launch_bounds__(256) quant_nvfp4_kernel(const QuantParams p, i
 
 namespace {
 template <int BN, int STAGES>
-cudaError_t launch_nvf4(const CUtensorMap& wmap, const CUtensorMap& xmap, const uint8_t* wsf, const uint8_t* xsf,
+cudaError_t launch_nvf4(const CUtensorMap& wmap, const CUtensorMap& xmap, const CUtensorMap& omap, const uint8_t* wsf,
+                        const uint8_t* xsf,
                         int sf_kbs, const GemmParams& p, int tiles_n, int tiles_m, int split, cudaStream_t stream,
                         bool pdl) {
   using C = Nvf4Cfg<BN, STAGES>;
@@ -299,7 +305,7 @@ cudaError_t launch_nvf4(const CUtensorMap& wmap, const CUtensorMap& xmap, const 
   }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(tiles_n, tiles_m, split);
-  cfg.blockDim = dim3(128, 1, 1);
+  cfg.blockDim = dim3(BN >= 128 ? 256 : 128, 1, 1);
   cfg.dynamicSmemBytes = C::SMEM;
   cfg.stream = stream;
   cudaLaunchAttribute attrs[2];
@@ -318,21 +324,22 @@ cudaError_t launch_nvf4(const CUtensorMap& wmap, const CUtensorMap& xmap, const 
   }
   cfg.attrs = attrs;
   cfg.numAttrs = na;
-  return cudaLaunchKernelEx(&cfg, kern, wmap, xmap, wsf, xsf, sf_kbs, p);
+  return cudaLaunchKernelEx(&cfg, kern, wmap, xmap, omap, wsf, xsf, sf_kbs, p);
 }
 }  // namespace
 
-cudaError_t launch_gemm_nvfp4(const CUtensorMap& wmap, const CUtensorMap& xmap, const uint8_t* wsf,
+cudaError_t launch_gemm_nvfp4(const CUtensorMap& wmap, const CUtensorMap& xmap, const CUtensorMap& omap,
+                              const uint8_t* wsf,
                               const uint8_t* xsf, int sf_kbs, const GemmParams& p, int bn, int split,
                               cudaStream_t stream, bool pdl) {
   const int tiles_n = p.N / 128;
   const int tiles_m = (p.M + bn - 1) / bn;
   if (p.N % 128 || split < 1 || split > 16 || split > p.kblocks) return cudaErrorInvalidValue;
   switch (bn) {
-    case 16: return launch_nvf4<16, 4>(wmap, xmap, wsf, xsf, sf_kbs, p, tiles_n, tiles_m, split, stream, pdl);
-    case 32: return launch_nvf4<32, 4>(wmap, xmap, wsf, xsf, sf_kbs, p, tiles_n, tiles_m, split, stream, pdl);
-    case 64: return launch_nvf4<64, 3>(wmap, xmap, wsf, xsf, sf_kbs, p, tiles_n, tiles_m, split, stream, pdl);
-    case 128: return launch_nvf4<128, 3>(wmap, xmap, wsf, xsf, sf_kbs, p, tiles_n, tiles_m, split, stream, pdl);
+    case 16: return launch_nvf4<16, 4>(wmap, xmap, omap, wsf, xsf, sf_kbs, p, tiles_n, tiles_m, split, stream, pdl);
+    case 32: return launch_nvf4<32, 4>(wmap, xmap, omap, wsf, xsf, sf_kbs, p, tiles_n, tiles_m, split, stream, pdl);
+    case 64: return launch_nvf4<64, 3>(wmap, xmap, omap, wsf, xsf, sf_kbs, p, tiles_n, tiles_m, split, stream, pdl);
+    case 128: return launch_nvf4<128, 3>(wmap, xmap, omap, wsf, xsf, sf_kbs, p, tiles_n, tiles_m, split, stream, pdl);
   }
   return cudaErrorInvalidValue;
 }

@@ -11,9 +11,10 @@ int gemm_token_tile(int M);
 void gemm_plan(int M, int N, int kblocks, int sm_count, int* bn, int* split);
 int gemm_k_elems(int kind);
 int gemm_split(int tiles, int kblocks, int sm_count, int max_split);
-cudaError_t launch_gemm(int kind, const CUtensorMap& wmap, const CUtensorMap& xmap, const GemmParams& p, int bn,
-                        int split, cudaStream_t stream, bool pdl);
-cudaError_t launch_gemm_nvfp4(const CUtensorMap& wmap, const CUtensorMap& xmap, const uint8_t* wsf,
+cudaError_t launch_gemm(int kind, const CUtensorMap& wmap, const CUtensorMap& xmap, const CUtensorMap& omap,
+                        const GemmParams& p, int bn, int split, cudaStream_t stream, bool pdl);
+cudaError_t launch_gemm_nvfp4(const CUtensorMap& wmap, const CUtensorMap& xmap, const CUtensorMap& omap,
+                              const uint8_t* wsf,
                               const uint8_t* xsf, int sf_kbs, const GemmParams& p, int bn, int split,
                               cudaStream_t stream, bool pdl);
 cudaError_t launch_nvfp4_pack_weight(const __nv_bfloat16* w, int rows, int k, unsigned int* amax_scratch, uint8_t* q,

@@ -32,6 +32,10 @@ struct GemmParams {
   const float* w_scale;     // fp8: per-feature fp32 scale [N]
   float w_tensor_scale;     // nvfp4: weight tensor scale
   uint32_t* status;         // device-visible status word
+  // 1: unsplit tiles use the TMA epilogue (the kernel's omap describes the
+  // output: bf16 [M][ldo] with a (128 | 64 for GEGLU) x BN box, or the fp32
+  // residual [M][ldr] with a 128 x BN box).
+  int tma_epilogue;
 };
 
 struct NormParams {
