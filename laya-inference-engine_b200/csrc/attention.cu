@@ -2,13 +2,21 @@
 // and the head's key-padded attention.  Replaces rope_qkv + SDPA
 // (src/laya_blackwell/model.py:92-96 and :62-67, kernels.py:62-93).
 //
-// One CTA = 64 queries of one (sequence, head); 4 warps x 16 queries.
-// Q and K are rotated while they are staged to shared memory, with the
-// reference's rounding: y = bf16(fl(a*cos) + fl(b*sin)) in fp32 without FMA
-// contraction.  Local layers only visit key tiles inside [q-64, q+64]
-// (compute skipping, not just masking).  Scores and the online softmax are
-// fp32; P is rounded to bf16 for the P.V product (as FlashAttention does);
-// a query that sees no key returns zeros (SDPA's result for a fully masked row).
+// One CTA = 64 queries of one (sequence, head); 4 warps x 16 queries, tensor
+// cores through mma.sync m16n8k16 (bf16, fp32 accumulate).  Local layers only
+// visit key tiles inside [q-64, q+64] (compute skipping, not just masking).
+// Scores and the online softmax are fp32; P is rounded to bf16 for the P.V
+// product (as FlashAttention does); a query that sees no key returns zeros
+// (SDPA's result for a fully masked row).
+//
+// Two load paths:
+//  * attention_kernel: Q and K are rotated while they are staged (batch-1
+//    shapes, where the QKV projection's split-K epilogue does not rotate):
+//    y = bf16(fl(a*cos) + fl(b*sin)) in fp32 without FMA contraction.
+//  * attention_async_kernel: the QKV projection already rotated q and k in its
+//    epilogue, so Q, K, V and the key-validity words are copied with cp.async
+//    (zero-filled past the sequence), the next key tile's copies in flight while
+//    the current tile is computed.
 #include "common.cuh"
 #include "params.h"
 #include "launch.h"
@@ -42,6 +50,18 @@ DEVI uint32_t pack_bf16(float lo, float hi) {
   return *reinterpret_cast<uint32_t*>(&v);
 }
 
+DEVI void cp_async16(void* dst, const void* src, bool valid) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(dst)), "l"(src), "r"(valid ? 16 : 0)
+               : "memory");
+}
+DEVI void cp_async4(void* dst, const void* src, bool valid) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"(smem_u32(dst)), "l"(src), "r"(valid ? 4 : 0)
+               : "memory");
+}
+DEVI void cp_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+DEVI void cp_wait_all_but_one() { asm volatile("cp.async.wait_group 1;" ::: "memory"); }
+DEVI void cp_wait_all() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
+
 // Rotate 8 dims [c, c+8) (c < 32) together with their partners [c+32, c+40).
 DEVI void rope8(uint4& lo, uint4& hi, const float* cs, const float* sn, int c) {
   __nv_bfloat16* xl = reinterpret_cast<__nv_bfloat16*>(&lo);
@@ -56,6 +76,133 @@ DEVI void rope8(uint4& lo, uint4& hi, const float* cs, const float* sn, int c) {
     xh[e] = __float2bfloat16_rn(yh);
   }
 }
+
+// Per-warp state of the online softmax for its 16 queries.
+struct Acc {
+  float o[8][4];
+  float mrow[2], lrow[2];
+};
+
+DEVI void acc_init(Acc& a) {
+#pragma unroll
+  for (int i = 0; i < 8; ++i) a.o[i][0] = a.o[i][1] = a.o[i][2] = a.o[i][3] = 0.f;
+  a.mrow[0] = a.mrow[1] = -INFINITY;
+  a.lrow[0] = a.lrow[1] = 0.f;
+}
+
+// Q fragments of this warp's 16 rows (4 k-steps of 16 dims).
+DEVI void load_q_frags(uint32_t (&qf)[4][4], const __nv_bfloat16* sQ, int warp, int lane) {
+#pragma unroll
+  for (int ks = 0; ks < 4; ++ks)
+    ldsm_x4(qf[ks], &sQ[(warp * 16 + (lane & 7) + ((lane >> 3) & 1) * 8) * LDS + ks * 16 + (lane >> 4) * 8]);
+}
+
+// One key tile (64 keys from position k0): scores, masking (key validity and
+// window), online-softmax update, O += P V.
+DEVI void attend_tile(Acc& acc, const uint32_t (&qf)[4][4], const __nv_bfloat16* sK, const __nv_bfloat16* sV,
+                      const int* kvalid, int k0, int window, int qpos0, int qpos1, int lane) {
+  const int t4 = lane & 3;
+  const float kScaleLog2 = 0.125f * 1.4426950408889634f;
+  float sc[8][4];
+#pragma unroll
+  for (int nt = 0; nt < 8; ++nt) {
+    sc[nt][0] = sc[nt][1] = sc[nt][2] = sc[nt][3] = 0.f;
+#pragma unroll
+    for (int kk = 0; kk < 2; ++kk) {
+      uint32_t kb[4];
+      ldsm_x4(kb, &sK[(nt * 8 + (lane & 7)) * LDS + kk * 32 + (lane >> 3) * 8]);
+      mma16816(sc[nt], qf[2 * kk], kb[0], kb[1]);
+      mma16816(sc[nt], qf[2 * kk + 1], kb[2], kb[3]);
+    }
+  }
+  float tmax[2] = {-INFINITY, -INFINITY};
+#pragma unroll
+  for (int nt = 0; nt < 8; ++nt) {
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const int kl = nt * 8 + 2 * t4 + (e & 1);
+      const int kp = k0 + kl;
+      const int qp = (e >> 1) ? qpos1 : qpos0;
+      bool vis = kvalid[kl] != 0 && qp >= 0;
+      if (window >= 0) vis = vis && abs(qp - kp) <= window;
+      const float v = vis ? sc[nt][e] * kScaleLog2 : -INFINITY;
+      sc[nt][e] = v;
+      tmax[e >> 1] = fmaxf(tmax[e >> 1], v);
+    }
+  }
+#pragma unroll
+  for (int r = 0; r < 2; ++r) {
+    tmax[r] = fmaxf(tmax[r], __shfl_xor_sync(0xffffffffu, tmax[r], 1));
+    tmax[r] = fmaxf(tmax[r], __shfl_xor_sync(0xffffffffu, tmax[r], 2));
+    const float mnew = fmaxf(acc.mrow[r], tmax[r]);
+    const float msafe = mnew == -INFINITY ? 0.f : mnew;
+    const float corr = exp2f(acc.mrow[r] - msafe);
+    acc.lrow[r] *= corr;
+#pragma unroll
+    for (int nt = 0; nt < 8; ++nt) {
+      acc.o[nt][2 * r] *= corr;
+      acc.o[nt][2 * r + 1] *= corr;
+    }
+    acc.mrow[r] = mnew;
+#pragma unroll
+    for (int nt = 0; nt < 8; ++nt) {
+      const float p0 = exp2f(sc[nt][2 * r] - msafe);
+      const float p1 = exp2f(sc[nt][2 * r + 1] - msafe);
+      sc[nt][2 * r] = p0;
+      sc[nt][2 * r + 1] = p1;
+      acc.lrow[r] += p0 + p1;
+    }
+  }
+#pragma unroll
+  for (int ks = 0; ks < 4; ++ks) {
+    uint32_t pa[4];
+    pa[0] = pack_bf16(sc[2 * ks][0], sc[2 * ks][1]);
+    pa[1] = pack_bf16(sc[2 * ks][2], sc[2 * ks][3]);
+    pa[2] = pack_bf16(sc[2 * ks + 1][0], sc[2 * ks + 1][1]);
+    pa[3] = pack_bf16(sc[2 * ks + 1][2], sc[2 * ks + 1][3]);
+#pragma unroll
+    for (int nt2 = 0; nt2 < 4; ++nt2) {
+      uint32_t vb[4];
+      ldsm_x4_t(vb, &sV[(ks * 16 + (lane & 7) + ((lane >> 3) & 1) * 8) * LDS + nt2 * 16 + (lane >> 4) * 8]);
+      mma16816(acc.o[2 * nt2], pa, vb[0], vb[1]);
+      mma16816(acc.o[2 * nt2 + 1], pa, vb[2], vb[3]);
+    }
+  }
+}
+
+// Normalise and store this warp's 16 output rows.
+DEVI void store_rows(const Acc& acc, const AttnParams& p, int b, int q0, int h, int warp, int lane) {
+  const int g = lane >> 2, t4 = lane & 3;
+#pragma unroll
+  for (int r = 0; r < 2; ++r) {
+    float l = acc.lrow[r];
+    l += __shfl_xor_sync(0xffffffffu, l, 1);
+    l += __shfl_xor_sync(0xffffffffu, l, 2);
+    const float inv = l > 0.f ? 1.f / l : 0.f;
+    const int qi = q0 + warp * 16 + g + 8 * r;
+    if (qi < p.nq) {
+      __nv_bfloat16* dst = p.out + ((size_t)b * p.nq + qi) * p.ld_out + h * 64;
+#pragma unroll
+      for (int nt = 0; nt < 8; ++nt)
+        *reinterpret_cast<uint32_t*>(dst + nt * 8 + 2 * t4) =
+            pack_bf16(acc.o[nt][2 * r] * inv, acc.o[nt][2 * r + 1] * inv);
+    }
+  }
+}
+
+// Key range of the CTA's query tile: all keys, or the tiles covering
+// [q0 - window, q_last + window] on local layers.
+DEVI void key_range(const AttnParams& p, int q0, int& kbeg, int& kend) {
+  kbeg = 0;
+  kend = p.s;
+  if (p.window >= 0) {  // queries of this tile are positions q0 .. q0+63
+    const int qmax = min(q0 + AQ, p.nq) - 1;
+    kbeg = max(0, q0 - p.window);
+    kend = min(p.s, qmax + p.window + 1);
+    kbeg = (kbeg / AK) * AK;
+  }
+}
+
 }  // namespace
 
 __global__ void __launch_bounds__(128) attention_kernel(const AttnParams p) {
@@ -89,28 +236,16 @@ __global__ void __launch_bounds__(128) attention_kernel(const AttnParams p) {
     *reinterpret_cast<uint4*>(&sQ[r * LDS + c]) = lo;
     *reinterpret_cast<uint4*>(&sQ[r * LDS + c + 32]) = hi;
   }
-
-  int kbeg = 0, kend = p.s;
-  if (p.window >= 0) {  // queries of this tile are positions q0 .. q0+63
-    const int qmax = min(q0 + AQ, p.nq) - 1;
-    kbeg = max(0, q0 - p.window);
-    kend = min(p.s, qmax + p.window + 1);
-    kbeg = (kbeg / AK) * AK;
-  }
+  int kbeg, kend;
+  key_range(p, q0, kbeg, kend);
   __syncthreads();
 
   uint32_t qf[4][4];
-#pragma unroll
-  for (int ks = 0; ks < 4; ++ks)
-    ldsm_x4(qf[ks], &sQ[(warp * 16 + (lane & 7) + ((lane >> 3) & 1) * 8) * LDS + ks * 16 + (lane >> 4) * 8]);
-
-  const int g = lane >> 2, t4 = lane & 3;
+  load_q_frags(qf, sQ, warp, lane);
+  const int g = lane >> 2;
   const int qpos0 = s_qpos[warp * 16 + g], qpos1 = s_qpos[warp * 16 + g + 8];
-  const float kScaleLog2 = 0.125f * 1.4426950408889634f;
-  float o[8][4];
-#pragma unroll
-  for (int i = 0; i < 8; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
-  float mrow[2] = {-INFINITY, -INFINITY}, lrow[2] = {0.f, 0.f};
+  Acc acc;
+  acc_init(acc);
 
   for (int k0 = kbeg; k0 < kend; k0 += AK) {
     __syncthreads();
@@ -135,90 +270,77 @@ __global__ void __launch_bounds__(128) attention_kernel(const AttnParams p) {
     }
     if (tid < AK) s_kvalid[tid] = (k0 + tid < p.s) ? (p.key_valid[seq_base + k0 + tid] != 0) : 0;
     __syncthreads();
-
-    float sc[8][4];
-#pragma unroll
-    for (int nt = 0; nt < 8; ++nt) {
-      sc[nt][0] = sc[nt][1] = sc[nt][2] = sc[nt][3] = 0.f;
-#pragma unroll
-      for (int kk = 0; kk < 2; ++kk) {
-        uint32_t kb[4];
-        ldsm_x4(kb, &sK[(nt * 8 + (lane & 7)) * LDS + kk * 32 + (lane >> 3) * 8]);
-        mma16816(sc[nt], qf[2 * kk], kb[0], kb[1]);
-        mma16816(sc[nt], qf[2 * kk + 1], kb[2], kb[3]);
-      }
-    }
-    // mask, scale to log2 domain, tile row max
-    float tmax[2] = {-INFINITY, -INFINITY};
-#pragma unroll
-    for (int nt = 0; nt < 8; ++nt) {
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const int kl = nt * 8 + 2 * t4 + (e & 1);
-        const int kp = k0 + kl;
-        const int qp = (e >> 1) ? qpos1 : qpos0;
-        bool vis = s_kvalid[kl] && qp >= 0;
-        if (p.window >= 0) vis = vis && abs(qp - kp) <= p.window;
-        const float v = vis ? sc[nt][e] * kScaleLog2 : -INFINITY;
-        sc[nt][e] = v;
-        tmax[e >> 1] = fmaxf(tmax[e >> 1], v);
-      }
-    }
-#pragma unroll
-    for (int r = 0; r < 2; ++r) {
-      tmax[r] = fmaxf(tmax[r], __shfl_xor_sync(0xffffffffu, tmax[r], 1));
-      tmax[r] = fmaxf(tmax[r], __shfl_xor_sync(0xffffffffu, tmax[r], 2));
-      const float mnew = fmaxf(mrow[r], tmax[r]);
-      const float msafe = mnew == -INFINITY ? 0.f : mnew;
-      const float corr = exp2f(mrow[r] - msafe);
-      lrow[r] *= corr;
-#pragma unroll
-      for (int nt = 0; nt < 8; ++nt) {
-        o[nt][2 * r] *= corr;
-        o[nt][2 * r + 1] *= corr;
-      }
-      mrow[r] = mnew;
-#pragma unroll
-      for (int nt = 0; nt < 8; ++nt) {
-        const float p0 = exp2f(sc[nt][2 * r] - msafe);
-        const float p1 = exp2f(sc[nt][2 * r + 1] - msafe);
-        sc[nt][2 * r] = p0;
-        sc[nt][2 * r + 1] = p1;
-        lrow[r] += p0 + p1;
-      }
-    }
-    // O += P V
-#pragma unroll
-    for (int ks = 0; ks < 4; ++ks) {
-      uint32_t pa[4];
-      pa[0] = pack_bf16(sc[2 * ks][0], sc[2 * ks][1]);
-      pa[1] = pack_bf16(sc[2 * ks][2], sc[2 * ks][3]);
-      pa[2] = pack_bf16(sc[2 * ks + 1][0], sc[2 * ks + 1][1]);
-      pa[3] = pack_bf16(sc[2 * ks + 1][2], sc[2 * ks + 1][3]);
-#pragma unroll
-      for (int nt2 = 0; nt2 < 4; ++nt2) {
-        uint32_t vb[4];
-        ldsm_x4_t(vb, &sV[(ks * 16 + (lane & 7) + ((lane >> 3) & 1) * 8) * LDS + nt2 * 16 + (lane >> 4) * 8]);
-        mma16816(o[2 * nt2], pa, vb[0], vb[1]);
-        mma16816(o[2 * nt2 + 1], pa, vb[2], vb[3]);
-      }
-    }
+    attend_tile(acc, qf, sK, sV, s_kvalid, k0, p.window, qpos0, qpos1, lane);
   }
+  store_rows(acc, p, b, q0, h, warp, lane);
+}
 
-#pragma unroll
-  for (int r = 0; r < 2; ++r) {
-    float l = lrow[r];
-    l += __shfl_xor_sync(0xffffffffu, l, 1);
-    l += __shfl_xor_sync(0xffffffffu, l, 2);
-    const float inv = l > 0.f ? 1.f / l : 0.f;
-    const int qi = q0 + warp * 16 + g + 8 * r;
-    if (qi < p.nq) {
-      __nv_bfloat16* dst = p.out + ((size_t)b * p.nq + qi) * p.ld_out + h * 64;
-#pragma unroll
-      for (int nt = 0; nt < 8; ++nt)
-        *reinterpret_cast<uint32_t*>(dst + nt * 8 + 2 * t4) = pack_bf16(o[nt][2 * r] * inv, o[nt][2 * r + 1] * inv);
-    }
+__global__ void __launch_bounds__(128) attention_async_kernel(const AttnParams p) {
+  __shared__ __align__(16) __nv_bfloat16 sQ[AQ * LDS];
+  __shared__ __align__(16) __nv_bfloat16 sK[2][AK * LDS];
+  __shared__ __align__(16) __nv_bfloat16 sV[2][AK * LDS];
+  __shared__ __align__(16) int s_kvalid[2][AK];
+  __shared__ int s_qpos[AQ];
+
+  griddep_launch_dependents();
+  const int q0 = blockIdx.x * AQ, h = blockIdx.y, b = blockIdx.z;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  griddep_wait();
+
+  if (tid < AQ) {
+    const int qi = q0 + tid;
+    s_qpos[tid] = qi < p.nq ? (p.q_pos ? p.q_pos[b * p.nq + qi] : qi) : -1;
   }
+  __syncthreads();
+  const size_t seq_base = (size_t)b * p.s;
+  // Q: 64 rows x 8 chunks of 16 bytes
+  for (int it = tid; it < AQ * 8; it += 128) {
+    const int r = it >> 3, c = (it & 7) * 8;
+    const int pos = s_qpos[r];
+    const __nv_bfloat16* src = pos >= 0 ? p.qkv + (seq_base + pos) * p.ld_qkv + h * 64 + c : p.qkv;
+    cp_async16(&sQ[r * LDS + c], src, pos >= 0);
+  }
+  int kbeg, kend;
+  key_range(p, q0, kbeg, kend);
+  const int ntiles = (kend - kbeg + AK - 1) / AK;
+  auto issue_tile = [&](int t) {
+    const int k0 = kbeg + t * AK, buf = t & 1;
+    for (int it = tid; it < AK * 8; it += 128) {
+      const int r = it >> 3, c = (it & 7) * 8;
+      const int kp = k0 + r;
+      const bool ok = kp < p.s;
+      const __nv_bfloat16* row = ok ? p.qkv + (seq_base + kp) * p.ld_qkv : p.qkv;
+      cp_async16(&sK[buf][r * LDS + c], row + p.d + h * 64 + c, ok);
+      cp_async16(&sV[buf][r * LDS + c], row + 2 * p.d + h * 64 + c, ok);
+    }
+    if (tid < AK) {
+      const bool ok = k0 + tid < p.s;
+      cp_async4(&s_kvalid[buf][tid], ok ? p.key_valid + seq_base + k0 + tid : p.key_valid, ok);
+    }
+    cp_commit();
+  };
+  if (ntiles > 0) issue_tile(0);  // first group also carries Q
+  else cp_commit();
+
+  const int g = lane >> 2;
+  const int qpos0 = s_qpos[warp * 16 + g], qpos1 = s_qpos[warp * 16 + g + 8];
+  Acc acc;
+  acc_init(acc);
+  uint32_t qf[4][4];
+  for (int t = 0; t < ntiles; ++t) {
+    if (t + 1 < ntiles) {
+      issue_tile(t + 1);
+      cp_wait_all_but_one();
+    } else {
+      cp_wait_all();
+    }
+    __syncthreads();
+    if (t == 0) load_q_frags(qf, sQ, warp, lane);
+    attend_tile(acc, qf, sK[t & 1], sV[t & 1], s_kvalid[t & 1], kbeg + t * AK, p.window, qpos0, qpos1, lane);
+    __syncthreads();  // buffer t & 1 is refilled by the copies issued in the next iteration
+  }
+  cp_wait_all();
+  store_rows(acc, p, b, q0, h, warp, lane);
 }
 
 cudaError_t launch_attention(const AttnParams& p, int batch, int heads, cudaStream_t stream, bool pdl) {
@@ -232,7 +354,8 @@ cudaError_t launch_attention(const AttnParams& p, int batch, int heads, cudaStre
   attr.val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = &attr;
   cfg.numAttrs = pdl ? 1 : 0;
-  return cudaLaunchKernelEx(&cfg, attention_kernel, p);
+  if (p.cos) return cudaLaunchKernelEx(&cfg, attention_kernel, p);
+  return cudaLaunchKernelEx(&cfg, attention_async_kernel, p);
 }
 
 }  // namespace laya

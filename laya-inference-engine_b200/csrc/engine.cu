@@ -326,12 +326,15 @@ struct Fwd {
     e->launches++;
   }
 
-  void gemm(const Proj& w, const void* x, const float* x_scale, int M, int epi, __nv_bfloat16* out, int ldo,
-            float* resid, int ldr) {
-    if (!on(kCatGemm)) return;
+  // Returns true when the wide epilogue applied the rotary embedding
+  // (cos / sin given) to the output's q and k columns.
+  bool gemm(const Proj& w, const void* x, const float* x_scale, int M, int epi, __nv_bfloat16* out, int ldo,
+            float* resid, int ldr, const float* rope_cos = nullptr, const float* rope_sin = nullptr,
+            int rope_seq = 0) {
     const int kb = (w.K + gemm_k_elems(w.kind) - 1) / gemm_k_elems(w.kind);
     int bn = 0, split = 1;
     gemm_plan(M, w.N, kb, e->sm_count, &bn, &split);
+    if (!on(kCatGemm)) return split == 1 && bn >= 128 && rope_cos && epi == kEpiStore;
     const int esize = w.kind == kKindBf16 ? 2 : 1;
     CUtensorMap xmap = make_map(x, M, w.K, esize, bn);
     GemmParams p{};
@@ -350,14 +353,25 @@ struct Fwd {
     p.status = e->status_dev;
     CUtensorMap omap;
     memset(&omap, 0, sizeof(omap));
-    if (split == 1 && bn >= 128) p.tma_epilogue = output_map(&omap, p, bn);
+    if (split == 1 && bn >= 128) {
+      p.tma_epilogue = output_map(&omap, p, bn);
+      if (!p.tma_epilogue) fail("output tensor map rejected for a %dx%d projection", M, w.N);
+    }
+    const bool rotated = p.tma_epilogue && rope_cos && epi == kEpiStore;
+    if (rotated) {
+      p.rope_cos = rope_cos;
+      p.rope_sin = rope_sin;
+      p.rope_seq = rope_seq;
+      p.rope_cols = 2 * (w.N / 3);
+    }
     count(launch_gemm(w.kind, w.map, xmap, omap, p, bn, split, st, pdl()), "gemm launch");
+    return rotated;
   }
 
   // NVFP4 projection: quantise the bf16 operand per row (scale blocks laid
   // out for the GEMM's token tile), then the block-scaled GEMM.
-  void gemm_nv4(const Proj& w, const __nv_bfloat16* x, int M, int epi, __nv_bfloat16* out, int ldo, float* resid,
-                int ldr) {
+  bool gemm_nv4(const Proj& w, const __nv_bfloat16* x, int M, int epi, __nv_bfloat16* out, int ldo, float* resid,
+                int ldr, const float* rope_cos = nullptr, const float* rope_sin = nullptr, int rope_seq = 0) {
     const int kb = (w.K + 255) / 256;
     int bn = 0, split = 1;
     gemm_plan(M, w.N, kb, e->sm_count, &bn, &split);
@@ -366,6 +380,7 @@ struct Fwd {
       const int tiles = (w.N / 128) * ((M + bn - 1) / bn);
       split = gemm_split(tiles, kb, e->sm_count, 8);
     }
+    const bool wide = split == 1 && bn >= 128;
     if (on(kCatRows)) {
       QuantParams q{};
       q.rows = M;
@@ -376,7 +391,7 @@ struct Fwd {
       q.sf = e->x4sf;
       count(launch_quant_nvfp4(q, bn, 4 * kb, st, pdl()), "nvfp4 quant launch");
     }
-    if (!on(kCatGemm)) return;
+    if (!on(kCatGemm)) return wide && rope_cos && epi == kEpiStore;
     CUtensorMap xmap = make_map(e->x4, M, w.K / 2, 1, bn);
     GemmParams p{};
     p.M = M;
@@ -393,8 +408,19 @@ struct Fwd {
     p.status = e->status_dev;
     CUtensorMap omap;
     memset(&omap, 0, sizeof(omap));
-    if (split == 1 && bn >= 128) p.tma_epilogue = output_map(&omap, p, bn);
+    if (wide) {
+      p.tma_epilogue = output_map(&omap, p, bn);
+      if (!p.tma_epilogue) fail("output tensor map rejected for a %dx%d projection", M, w.N);
+    }
+    const bool rotated = p.tma_epilogue && rope_cos && epi == kEpiStore;
+    if (rotated) {
+      p.rope_cos = rope_cos;
+      p.rope_sin = rope_sin;
+      p.rope_seq = rope_seq;
+      p.rope_cols = 2 * (w.N / 3);
+    }
     count(launch_gemm_nvfp4(w.map, xmap, omap, w.wsf, e->x4sf, kb, p, bn, split, st, pdl()), "nvfp4 gemm launch");
+    return rotated;
   }
 
   // Output tensor map of the TMA epilogue (unsplit tiles).
@@ -467,11 +493,15 @@ struct Fwd {
         }
         norm(p);
       }
-      if (nv4)
-        gemm_nv4(E.wqkv[i], E.n, T, kEpiStore, E.qkv, 3 * d, nullptr, 0);
-      else
-        gemm(E.wqkv[i], fp8 ? (const void*)E.n8 : (const void*)E.n, E.n8s, T, kEpiStore, E.qkv, 3 * d, nullptr, 0);
       const bool glob = (i % c.global_every) == 0;
+      const float* rc = glob ? E.gcos : E.lcos;
+      const float* rs = glob ? E.gsin : E.lsin;
+      // The rotary embedding runs in the projection's epilogue when it uses
+      // the wide (unsplit, 128-token) epilogue, else in the attention kernel.
+      const bool rotated =
+          nv4 ? gemm_nv4(E.wqkv[i], E.n, T, kEpiStore, E.qkv, 3 * d, nullptr, 0, rc, rs, s)
+              : gemm(E.wqkv[i], fp8 ? (const void*)E.n8 : (const void*)E.n, E.n8s, T, kEpiStore, E.qkv, 3 * d,
+                     nullptr, 0, rc, rs, s);
       {
         AttnParams a{};
         a.qkv = E.qkv;
@@ -480,8 +510,8 @@ struct Fwd {
         a.s = s;
         a.nq = s;
         a.key_valid = valid;
-        a.cos = glob ? E.gcos : E.lcos;
-        a.sin = glob ? E.gsin : E.lsin;
+        a.cos = rotated ? nullptr : rc;
+        a.sin = rotated ? nullptr : rs;
         a.window = glob ? -1 : c.local_window;
         a.out = E.attn;
         a.ld_out = d;

@@ -280,7 +280,32 @@ DEVI void tile_epilogue_wide(const GemmParams& p, const CUtensorMap* omap, uint3
       }
     }
     __nv_bfloat16 o[4];
-    if (ep == kEpiGeglu) {
+    if (n < p.rope_cols) {
+      // bf16(qkv) rotated in fp32 without FMA, as rope_qkv does (kernels.py:62-93)
+      const int d0 = r0 & 63;
+      const int pr = d0 < 32 ? r0 + 32 : r0 - 32;
+      const float4 pb = *reinterpret_cast<const float4*>(P + tok * 128 + pr);
+      float y[4] = {pb.x, pb.y, pb.z, pb.w};
+      if (KIND == kKindFp8) {
+        const float4 w = *reinterpret_cast<const float4*>(p.w_scale + tile_n * 128 + pr);
+        const float ww[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) y[e] = (y[e] * S[tok]) * ww[e];
+      } else if (KIND == kKindNvfp4) {
+#pragma unroll
+        for (int e = 0; e < 4; ++e) y[e] *= S[tok] * tsc;
+      }
+      const int pos = (m_base + tok) % p.rope_seq;
+      const float* cs = p.rope_cos + (size_t)pos * 64 + d0;
+      const float* sn = p.rope_sin + (size_t)pos * 64 + d0;
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float a = bf16_round(x[e]), b = bf16_round(y[e]);
+        const float rot = __fmul_rn(d0 < 32 ? -b : b, sn[e]);
+        o[e] = __float2bfloat16_rn(__fadd_rn(__fmul_rn(a, cs[e]), rot));
+      }
+      *reinterpret_cast<uint2*>(O + tok * 128 + r0) = *reinterpret_cast<uint2*>(o);
+    } else if (ep == kEpiGeglu) {
 #pragma unroll
       for (int e = 0; e < 4; ++e)
         o[e] = __float2bfloat16_rn(bf16_round(gelu_erf(bf16_round(x[e]))) * bf16_round(g[e]));

@@ -36,6 +36,13 @@ struct GemmParams {
   // output: bf16 [M][ldo] with a (128 | 64 for GEGLU) x BN box, or the fp32
   // residual [M][ldr] with a 128 x BN box).
   int tma_epilogue;
+  // Rotary embedding applied in the wide epilogue to output columns
+  // [0, rope_cols) (q and k of a QKV projection): position = row % rope_seq,
+  // tables [max_len][64].  rope_cols = 0 disables it.
+  const float* rope_cos;
+  const float* rope_sin;
+  int rope_seq;
+  int rope_cols;
 };
 
 struct NormParams {
