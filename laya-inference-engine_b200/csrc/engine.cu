@@ -132,6 +132,10 @@ struct Shape {
   int b, s, k, unmasked;
 };
 
+// Capacity of the split-K partial scratch (floats): larger reductions fall
+// back to distributed shared memory.
+constexpr size_t kPartialFloats = (size_t)16 * 1024 * 1024;
+
 // Compact per-shape layout of the int32 input words and fp32 output words, so
 // each step copies only what the shape needs.
 struct IoLayout {
@@ -201,6 +205,7 @@ struct laya_b200_engine {
   uint8_t* x4sf = nullptr;          // nvfp4 activation scale blocks
   float* x4o = nullptr;             // nvfp4 per-row outer scales [T]
   int x4_col_blocks = 0;
+  float* gpart = nullptr;           // split-K partials of the cluster reduction (kPartialFloats)
   float* a1 = nullptr;              // tail scratch [max_batch][act_hidden]
   unsigned int* arrivals = nullptr; // tail arrival counters [max_batch]
   // device inputs / outputs (int32 staging layout)
@@ -353,6 +358,8 @@ struct Fwd {
     p.status = e->status_dev;
     CUtensorMap omap;
     memset(&omap, 0, sizeof(omap));
+    if (split > 1 && (size_t)(w.N / 128) * ((M + bn - 1) / bn) * split * bn * 128 <= kPartialFloats)
+      p.partials = e->gpart;
     if (split == 1 && bn >= 128) {
       p.tma_epilogue = output_map(&omap, p, bn);
       if (!p.tma_epilogue) fail("output tensor map rejected for a %dx%d projection", M, w.N);
@@ -813,6 +820,7 @@ int laya_b200_create(int device, const laya_b200_config* cfg, laya_b200_engine**
         {(void**)&e->gsin, (size_t)c.max_len * 64 * 4}, {(void**)&e->lcos, (size_t)c.max_len * 64 * 4},
         {(void**)&e->lsin, (size_t)c.max_len * 64 * 4},
         {(void**)&e->a1, (size_t)c.max_batch * c.act_hidden * 4},
+        {(void**)&e->gpart, kPartialFloats * 4},
         {(void**)&e->x4, T * (size_t)(d > I ? d : I) / 2},
         {(void**)&e->x4sf, ((T + 15) / 16) * (size_t)(4 * ((std::max(d, I) + 255) / 256)) * 512},
         {(void**)&e->x4o, T * 4},

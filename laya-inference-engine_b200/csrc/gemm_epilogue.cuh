@@ -92,6 +92,11 @@ DEVI void tile_epilogue(const GemmParams& p, uint32_t tmem, float* part, int til
                         int rank) {
   const int tid = threadIdx.x, warp = tid >> 5;
   const uint32_t lane_addr = tmem + ((uint32_t)(warp * 32) << 16);
+  // Split-K partials go to a global (L2) scratch when one is given: peers then
+  // read them after the cluster barrier, and no closing barrier is needed to
+  // keep a CTA's shared memory alive for its readers.
+  const bool gpath = split > 1 && p.partials != nullptr;
+  if (gpath) part = p.partials + ((size_t)(tile_m * gridDim.x + tile_n) * split + rank) * BN * 128;
   if (tid >= 128) {
     // CTAs of more than 128 threads: only warps 0-3 own TMEM lanes
   } else if (BN >= 32) {
@@ -141,9 +146,15 @@ DEVI void tile_epilogue(const GemmParams& p, uint32_t tmem, float* part, int til
 #pragma unroll
         for (int u = 0; u < 8; ++u)
           if (q0 + u < split) {
-            const uint32_t base = mapa_shared(part_addr, (uint32_t)(q0 + u));
-            va[u] = ld_dsmem_f32x4(base + off * 4);
-            vb[u] = ld_dsmem_f32x4(base + (off + 64) * 4);
+            if (gpath) {  // L2 loads (the cluster barrier ordered the peers' stores)
+              const float* src = p.partials + ((size_t)(tile_m * gridDim.x + tile_n) * split + q0 + u) * BN * 128 + off;
+              va[u] = __ldcg(reinterpret_cast<const float4*>(src));
+              vb[u] = __ldcg(reinterpret_cast<const float4*>(src + 64));
+            } else {
+              const uint32_t base = mapa_shared(part_addr, (uint32_t)(q0 + u));
+              va[u] = ld_dsmem_f32x4(base + off * 4);
+              vb[u] = ld_dsmem_f32x4(base + (off + 64) * 4);
+            }
           }
 #pragma unroll
         for (int u = 0; u < 8; ++u)
@@ -155,7 +166,7 @@ DEVI void tile_epilogue(const GemmParams& p, uint32_t tmem, float* part, int til
     }
     epilogue_quad<KIND>(p, m, tile_n * 128 + q4, tile_n * 64 + q4, lo, hi);
   }
-  if (split > 1) cluster_sync_all();
+  if (split > 1 && !gpath) cluster_sync_all();
 
 }
 

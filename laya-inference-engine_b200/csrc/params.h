@@ -43,6 +43,7 @@ struct GemmParams {
   const float* rope_sin;
   int rope_seq;
   int rope_cols;
+  float* partials;           // global split-K partials [tiles][split][BN][128] floats, or null
 };
 
 struct NormParams {
