@@ -82,7 +82,8 @@ LAYA_B200_API int laya_b200_run(laya_b200_engine* e, int slot, const int64_t* in
  * and write each replay's device time in milliseconds (CUDA events on the
  * engine's stream) to ms_each[iterations].  kernel_mask selects the kernel
  * families in the replayed graph: 1 projections (GEMM), 2 attention, 4 row
- * kernels (norms, quantisation, gather, tail); 7 is the whole forward.
+ * kernels (norms, gather, tail), 8 activation quantisers (FP8 / NVFP4);
+ * 15 is the whole forward.
  * Partial masks compute garbage and exist only to time one family. */
 LAYA_B200_API int laya_b200_replay_device(laya_b200_engine* e, int slot, int iterations, int kernel_mask,
                                           float* ms_each);
@@ -92,8 +93,9 @@ LAYA_B200_API int laya_b200_kernel_count(laya_b200_engine* e, int slot, int* cou
 
 /* Test hook with no counterpart in the reference: copy the first `bytes` of
  * a named activation buffer ("h", "n", "qkv", "attn", "g", "hsel", "msc",
- * "zsc") to host memory after synchronising, so kernel-level tests can
- * compare intermediate results with a CPU oracle. */
+ * "zsc"; with FP8 also the e4m3 codes and per-row scales "n8", "n8s", "a8",
+ * "a8s", "g8", "g8s") to host memory after synchronising, so kernel-level
+ * tests can compare intermediate results with a CPU oracle. */
 LAYA_B200_API int laya_b200_read_buffer(laya_b200_engine* e, const char* name, void* dst, size_t bytes);
 
 /* Arguments of laya_b200_tail_noalloc: device pointers the caller owns. */

@@ -263,6 +263,19 @@ DEVI uint8_t f32x2_to_e2m1x2(float lo, float hi) {
   return (uint8_t)(r & 0xFF);
 }
 
+// x / d rounded to nearest, given inv = 1/d rounded to nearest, by two
+// residual corrections of the product x * inv (Markstein's FMA division,
+// IBM J. Res. Dev. 34(1):111-119, 1990): after the first step the quotient is
+// faithful, and a correction of a faithful quotient with an exact residual
+// r = x - q*d and a correctly rounded reciprocal yields the correctly rounded
+// quotient.  Valid for normal d and quotients that neither overflow nor
+// underflow; the quantisers divide by scales >= 1e-12 with |x| <= 448 * d.
+DEVI float div_rn_by(float x, float d, float inv) {
+  float q = x * inv;
+  q = fmaf(fmaf(-q, d, x), inv, q);
+  return fmaf(fmaf(-q, d, x), inv, q);
+}
+
 DEVI float warp_sum(float v) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);

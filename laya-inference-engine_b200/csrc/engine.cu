@@ -162,12 +162,12 @@ IoLayout io_layout(const Shape& sh) {
 }
 
 // Kernel categories for partial replays (timing of one kernel family).
-enum : int { kCatGemm = 1, kCatAttention = 2, kCatRows = 4, kCatAll = 7 };
+enum : int { kCatGemm = 1, kCatAttention = 2, kCatRows = 4, kCatQuant = 8, kCatAll = 15 };
 
 struct Slot {
   Shape sh;
   cudaGraphExec_t io_exec = nullptr;   // H2D + kernels + D2H
-  cudaGraphExec_t dev_exec[8] = {};    // kernels only, by category mask
+  cudaGraphExec_t dev_exec[16] = {};    // kernels only, by category mask
   int kernels = 0;
   bool live = false;
 };
@@ -388,7 +388,7 @@ struct Fwd {
       split = gemm_split(tiles, kb, e->sm_count, 8);
     }
     const bool wide = split == 1 && bn >= 128;
-    if (on(kCatRows)) {
+    if (on(kCatQuant)) {
       QuantParams q{};
       q.rows = M;
       q.k = w.K;
@@ -524,7 +524,7 @@ struct Fwd {
         a.ld_out = d;
         attention(a, b, c.heads);
       }
-      if (fp8 && on(kCatRows)) {
+      if (fp8 && on(kCatQuant)) {
         QuantParams q{};
         q.rows = T;
         q.k = d;
@@ -555,7 +555,7 @@ struct Fwd {
         gemm_nv4(E.wi[i], E.n, T, kEpiGeglu, E.g, I, nullptr, 0);
       else
         gemm(E.wi[i], fp8 ? (const void*)E.n8 : (const void*)E.n, E.n8s, T, kEpiGeglu, E.g, I, nullptr, 0);
-      if (fp8 && on(kCatRows)) {
+      if (fp8 && on(kCatQuant)) {
         QuantParams q{};
         q.rows = T;
         q.k = I;
@@ -908,6 +908,7 @@ int laya_b200_finalize(laya_b200_engine* e, int precision) {
     const laya_b200_config& c = e->cfg;
     const int kind = precision == LAYA_B200_FP8 ? kKindFp8 : precision == LAYA_B200_NVFP4 ? kKindNvfp4 : kKindBf16;
     if (kind == kKindNvfp4 && (c.hidden % 16 || c.intermediate % 16)) fail("NVFP4 needs K divisible by 16");
+    if (kind == kKindFp8 && c.intermediate > 4096) fail("FP8 needs intermediate <= 4096 (row quantiser width)");
     std::vector<std::pair<std::string, size_t>> qoff;  // weight name -> offset of e4m3 bytes, scales follow
     if (kind == kKindFp8) {
       size_t off = 0;
@@ -1139,6 +1140,12 @@ int laya_b200_read_buffer(laya_b200_engine* e, const char* name, void* dst, size
     else if (n == "hsel") { src = e->hsel; cap = R * d * 4; }
     else if (n == "msc") { src = e->msc; cap = BK * d * 2; }
     else if (n == "zsc") { src = e->zsc; cap = BK * d * 2; }
+    else if (n == "n8" && e->n8) { src = e->n8; cap = T * d; }
+    else if (n == "n8s" && e->n8s) { src = e->n8s; cap = T * 4; }
+    else if (n == "a8" && e->a8) { src = e->a8; cap = T * d; }
+    else if (n == "a8s" && e->a8s) { src = e->a8s; cap = T * 4; }
+    else if (n == "g8" && e->g8) { src = e->g8; cap = T * (size_t)c.intermediate; }
+    else if (n == "g8s" && e->g8s) { src = e->g8s; cap = T * 4; }
     else fail("unknown buffer %s", name);
     if (bytes > cap) fail("buffer %s holds %zu bytes, %zu requested", name, cap, bytes);
     ck(cudaStreamSynchronize(e->stream), "sync");

@@ -134,7 +134,10 @@ __global__ void __launch_bounds__(BN >= 128 ? 256 : 128, BN == 128 ? 2 : 1)
         else
           umma_f8(tmem, ad + 2 * k, bd + 2 * k, idesc, (i | k) != 0);
       }
-      umma_commit(&empty[s]);
+      // Only stages that the producer refills get a release; the last STAGES
+      // k-blocks are covered by `done`, so no arrive is left in flight when
+      // the CTA exits.
+      if (i + STAGES < nkb) umma_commit(&empty[s]);
     }
     umma_commit(done);
   }

@@ -97,6 +97,8 @@ DEVI void tile_epilogue(const GemmParams& p, uint32_t tmem, float* part, int til
   // keep a CTA's shared memory alive for its readers.
   const bool gpath = split > 1 && p.partials != nullptr;
   if (gpath) part = p.partials + ((size_t)(tile_m * gridDim.x + tile_n) * split + rank) * BN * 128;
+  // CTA `rank` owns the tokens [t0, t1) of the tile in the reduction below.
+  const int t0 = rank * BN / split, t1 = (rank + 1) * BN / split, nt = t1 - t0;
   if (tid >= 128) {
     // CTAs of more than 128 threads: only warps 0-3 own TMEM lanes
   } else if (BN >= 32) {
@@ -121,11 +123,9 @@ DEVI void tile_epilogue(const GemmParams& p, uint32_t tmem, float* part, int til
   else
     __syncthreads();
 
-  // ---- reduction over the cluster and the epilogue.  CTA `rank` owns the
-  // tokens [t0, t1) of the tile; a thread takes 4 consecutive rows (and their
-  // +64 partners) of one token and sums the S partials in rank order with
-  // 16-byte DSMEM loads issued back to back.
-  const int t0 = rank * BN / split, t1 = (rank + 1) * BN / split, nt = t1 - t0;
+  // ---- reduction over the cluster and the epilogue: a thread takes 4
+  // consecutive rows (and their +64 partners) of one token and sums the S
+  // partials in rank order with 16-byte loads issued back to back.
   const uint32_t part_addr = smem_u32(part);
   for (int item = tid; tid < 128 && item < nt * 16; item += 128) {
     const int tl = t0 + (item >> 4);

@@ -168,7 +168,10 @@ __global__ void __launch_bounds__(BN >= 128 ? 256 : 128, BN == 128 ? 2 : 1)
 #pragma unroll
       for (int j = 0; j < 4; ++j)  // K = 64 elements = 32 bytes per MMA
         umma_nvf4(tmem, ad + 2 * j, bd + 2 * j, idesc, t_sfa + 4 * j, t_sfb + 4 * j, (i | j) != 0);
-      umma_commit(&empty[s]);
+      // Only stages that the producer refills get a release; the last STAGES
+      // k-blocks are covered by `done`, so no arrive is left in flight when
+      // the CTA exits.
+      if (i + STAGES < nkb) umma_commit(&empty[s]);
     }
     umma_commit(done);
   }
@@ -185,6 +188,7 @@ __global__ void __launch_bounds__(BN >= 128 ? 256 : 128, BN == 128 ? 2 : 1)
   else
     tile_epilogue<BN, kKindNvfp4>(p, tmem, reinterpret_cast<float*>(smem), tile_n, tile_m, split, rank);
 
+  // ---- teardown: drain copies still in flight after a failure, free TMEM
   if (tid == 0 && *failed) {
     for (int i = (issued > STAGES ? issued - STAGES : 0); i < issued; ++i)
       mbar_wait(&full[i % STAGES], (i / STAGES) & 1);

@@ -106,14 +106,14 @@ __global__ void __launch_bounds__(256) norm_kernel(const NormParams p) {
   }
   if (p.out_fp8) {
     amax = warp_max(amax);
-    const float scale = fmaxf(amax / 448.0f, 1e-12f);
+    const float scale = fmaxf(amax / 448.0f, 1e-12f), inv = 1.0f / scale;
     uint8_t* dst = p.out_fp8 + (size_t)row * p.d;
 #pragma unroll
     for (int i = 0; i < NV; ++i) {
-      const float a = fminf(fmaxf(x[i].x / scale, -448.f), 448.f);
-      const float bq = fminf(fmaxf(x[i].y / scale, -448.f), 448.f);
-      const float c = fminf(fmaxf(x[i].z / scale, -448.f), 448.f);
-      const float e = fminf(fmaxf(x[i].w / scale, -448.f), 448.f);
+      const float a = fminf(fmaxf(div_rn_by(x[i].x, scale, inv), -448.f), 448.f);
+      const float bq = fminf(fmaxf(div_rn_by(x[i].y, scale, inv), -448.f), 448.f);
+      const float c = fminf(fmaxf(div_rn_by(x[i].z, scale, inv), -448.f), 448.f);
+      const float e = fminf(fmaxf(div_rn_by(x[i].w, scale, inv), -448.f), 448.f);
       const uint32_t lo = f32x2_to_e4m3x2(a, bq), hi = f32x2_to_e4m3x2(c, e);
       *reinterpret_cast<uint32_t*>(dst + (lane + 32 * i) * 4) = lo | (hi << 16);
     }
@@ -121,7 +121,10 @@ __global__ void __launch_bounds__(256) norm_kernel(const NormParams p) {
   }
 }
 
-// Per-row e4m3 quantisation of a bf16 matrix (quantization.py:20-29).
+// Per-row e4m3 quantisation of a bf16 matrix (quantization.py:20-29).  The
+// warp's row (k <= 256*MAXC) is loaded into registers with all loads in
+// flight at once, so a short batch pays one memory latency, not one per chunk.
+template <int MAXC>
 __global__ void __launch_bounds__(256) quant_fp8_kernel(const QuantParams p) {
   griddep_launch_dependents();
   griddep_wait();
@@ -129,25 +132,34 @@ __global__ void __launch_bounds__(256) quant_fp8_kernel(const QuantParams p) {
   const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   if (row >= p.rows) return;
   const __nv_bfloat16* src = p.src + (size_t)row * p.k;
+  uint4 u[MAXC];
+#pragma unroll
+  for (int i = 0; i < MAXC; ++i) {
+    const int c = lane * 8 + 256 * i;
+    u[i] = c < p.k ? *reinterpret_cast<const uint4*>(src + c) : make_uint4(0, 0, 0, 0);
+  }
   float amax = 0.f;
-  for (int c = lane * 8; c < p.k; c += 256) {
-    const uint4 u = *reinterpret_cast<const uint4*>(src + c);
-    const __nv_bfloat16* e = reinterpret_cast<const __nv_bfloat16*>(&u);
+#pragma unroll
+  for (int i = 0; i < MAXC; ++i) {
+    const __nv_bfloat16* e = reinterpret_cast<const __nv_bfloat16*>(&u[i]);
 #pragma unroll
     for (int j = 0; j < 8; ++j) amax = fmaxf(amax, fabsf(__bfloat162float(e[j])));
   }
   amax = warp_max(amax);
-  const float scale = fmaxf(amax / 448.0f, 1e-12f);
+  const float scale = fmaxf(amax / 448.0f, 1e-12f), inv = 1.0f / scale;
   uint8_t* dst = p.q + (size_t)row * p.k;
-  for (int c = lane * 8; c < p.k; c += 256) {
-    const uint4 u = *reinterpret_cast<const uint4*>(src + c);
-    const __nv_bfloat16* e = reinterpret_cast<const __nv_bfloat16*>(&u);
+#pragma unroll
+  for (int i = 0; i < MAXC; ++i) {
+    const int c = lane * 8 + 256 * i;
+    if (c >= p.k) continue;
+    const __nv_bfloat16* e = reinterpret_cast<const __nv_bfloat16*>(&u[i]);
     uint32_t w[2];
 #pragma unroll
     for (int j = 0; j < 2; ++j) {
       float v[4];
 #pragma unroll
-      for (int t = 0; t < 4; ++t) v[t] = fminf(fmaxf(__bfloat162float(e[4 * j + t]) / scale, -448.f), 448.f);
+      for (int t = 0; t < 4; ++t)
+        v[t] = fminf(fmaxf(div_rn_by(__bfloat162float(e[4 * j + t]), scale, inv), -448.f), 448.f);
       w[j] = (uint32_t)f32x2_to_e4m3x2(v[0], v[1]) | ((uint32_t)f32x2_to_e4m3x2(v[2], v[3]) << 16);
     }
     *reinterpret_cast<uint2*>(dst + c) = make_uint2(w[0], w[1]);
@@ -323,10 +335,14 @@ cudaError_t launch_norm(const NormParams& p, cudaStream_t stream, bool pdl) {
 }
 
 cudaError_t launch_quant_fp8(const QuantParams& p, cudaStream_t stream, bool pdl) {
-  if (p.k % 8) return cudaErrorInvalidValue;
+  if (p.k % 8 || p.k > 4096) return cudaErrorInvalidValue;
   QuantParams q = p;
   void* args[] = {&q};
-  return launch_rows((const void*)quant_fp8_kernel, args, p.rows, 0, stream, pdl);
+  const void* kern = p.k <= 1024   ? (const void*)quant_fp8_kernel<4>
+                     : p.k <= 2048 ? (const void*)quant_fp8_kernel<8>
+                     : p.k <= 3072 ? (const void*)quant_fp8_kernel<12>
+                                   : (const void*)quant_fp8_kernel<16>;
+  return launch_rows(kern, args, p.rows, 0, stream, pdl);
 }
 
 cudaError_t launch_gather_rows(float* dst, const float* src, const int* map, int rows, int d, cudaStream_t stream,

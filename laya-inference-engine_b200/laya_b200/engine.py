@@ -99,7 +99,7 @@ class NativeForward:
         _lib.check(self.lib, self.handle, st, "run")
         return logits, act
 
-    def replay_device(self, slot, iterations, kernel_mask=7):
+    def replay_device(self, slot, iterations, kernel_mask=15):
         """Per-replay device milliseconds of `iterations` back-to-back replays."""
         ms = np.empty(iterations, dtype=np.float32)
         st = self.lib.laya_b200_replay_device(self.handle, slot, iterations, kernel_mask,

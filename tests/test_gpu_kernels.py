@@ -157,3 +157,30 @@ def test_low_precision_qkv_stage_matches_oracle(precision):
     mm = inp["marker_mask"]
     tol = {"fp8": 6e-2, "nvfp4": 1.5e-1}[precision]
     assert np.abs(logits[mm] - ol[mm]).max() <= tol and np.abs(act - oa).max() <= tol
+
+
+@pytest.mark.parametrize("intermediate", [384, 1920, 2624, 4096])
+def test_fp8_activation_quantiser_is_bit_exact(intermediate):
+    """The per-row e4m3 activation quantiser (quantization.py:20-29) on the
+    attention output (k = hidden) and the GEGLU output (k = intermediate)
+    against the oracle's torch restatement: scales and codes identical."""
+    from laya_b200.engine import NativeForward
+    cfg = LayaConfig(layers=1, hidden=256, heads=4, intermediate=intermediate, vocab=1000, pad_token_id=999,
+                     max_len=512, head_layers=0, head_heads=4, head_ff=512, act_hidden=64)
+    w = seeded_weights(cfg, seed=5)
+    nf = NativeForward(0, cfg, w, "fp8", max_batch=4, max_options=8)
+    try:
+        b, s, k = 2, 128, 4
+        items = synthetic_items([128, 77], ["choice", "score"], seed=12, vocab=cfg.vocab)
+        nf.run(nf.capture(b, s, k, False), pack(items, b, s, k, cfg.pad_token_id))
+        T = b * s
+        for src, q, sc, width in (("attn", "a8", "a8s", cfg.hidden), ("g", "g8", "g8s", intermediate)):
+            x = bf16_of(nf.read_buffer(src, (T, width), np.uint16))
+            codes = torch.from_numpy(nf.read_buffer(q, (T, width), np.uint8))
+            scale = torch.from_numpy(nf.read_buffer(sc, (T,), np.float32))
+            ref_q, ref_scale = O.fp8_quantize_rows(x)
+            assert torch.equal(scale, ref_scale[:, 0]), src
+            got = codes.view(torch.float8_e4m3fn).to(torch.float32)
+            assert torch.equal(got, ref_q), (src, int((got != ref_q).sum()))
+    finally:
+        nf.close()
