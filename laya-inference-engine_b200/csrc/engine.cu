@@ -331,15 +331,15 @@ struct Fwd {
     e->launches++;
   }
 
-  // Returns true when the wide epilogue applied the rotary embedding
-  // (cos / sin given) to the output's q and k columns.
+  // Returns true when the epilogue applied the rotary embedding (cos / sin
+  // given, plain store) to the output's q and k columns.
   bool gemm(const Proj& w, const void* x, const float* x_scale, int M, int epi, __nv_bfloat16* out, int ldo,
             float* resid, int ldr, const float* rope_cos = nullptr, const float* rope_sin = nullptr,
             int rope_seq = 0) {
     const int kb = (w.K + gemm_k_elems(w.kind) - 1) / gemm_k_elems(w.kind);
     int bn = 0, split = 1;
     gemm_plan(M, w.N, kb, e->sm_count, &bn, &split);
-    if (!on(kCatGemm)) return split == 1 && bn >= 128 && rope_cos && epi == kEpiStore;
+    if (!on(kCatGemm)) return rope_cos && epi == kEpiStore;
     const int esize = w.kind == kKindBf16 ? 2 : 1;
     CUtensorMap xmap = make_map(x, M, w.K, esize, bn);
     GemmParams p{};
@@ -364,7 +364,7 @@ struct Fwd {
       p.tma_epilogue = output_map(&omap, p, bn);
       if (!p.tma_epilogue) fail("output tensor map rejected for a %dx%d projection", M, w.N);
     }
-    const bool rotated = p.tma_epilogue && rope_cos && epi == kEpiStore;
+    const bool rotated = rope_cos && epi == kEpiStore;
     if (rotated) {
       p.rope_cos = rope_cos;
       p.rope_sin = rope_sin;
@@ -373,6 +373,33 @@ struct Fwd {
     }
     count(launch_gemm(w.kind, w.map, xmap, omap, p, bn, split, st, pdl()), "gemm launch");
     return rotated;
+  }
+
+  // Attention fused into the residual output projection (bf16, one sequence of
+  // 32 < s <= 64 tokens with q and k already rotated, each CTA's K slice at
+  // most four heads).  Returns false,
+  // launching nothing, when the shape does not qualify.
+  bool gemm_attn(const Proj& w, const AttnParams& a, int M) {
+    if (w.kind != kKindBf16 || a.q_pos || a.nq != a.s || a.s != M || M <= 32 || M > 64 || w.K % 64 || a.cos)
+      return false;
+    const int kb = w.K / 64;
+    int bn = 0, split = 1;
+    gemm_plan(M, w.N, kb, e->sm_count, &bn, &split);
+    if (bn != 64 || (kb + split - 1) / split > 4) return false;
+    if (!on(kCatGemm)) return true;
+    GemmParams p{};
+    p.M = M;
+    p.N = w.N;
+    p.K = w.K;
+    p.kblocks = kb;
+    p.epilogue = kEpiResidual;
+    p.resid = e->h;
+    p.ldr = e->cfg.hidden;
+    p.bias = w.bias;
+    p.status = e->status_dev;
+    if (split > 1 && (size_t)(w.N / 128) * split * bn * 128 <= kPartialFloats) p.partials = e->gpart;
+    count(launch_gemm_attn(w.map, p, a, split, st, pdl()), "fused attention launch");
+    return true;
   }
 
   // NVFP4 projection: quantise the bf16 operand per row (scale blocks laid
@@ -398,7 +425,7 @@ struct Fwd {
       q.sf = e->x4sf;
       count(launch_quant_nvfp4(q, bn, 4 * kb, st, pdl()), "nvfp4 quant launch");
     }
-    if (!on(kCatGemm)) return wide && rope_cos && epi == kEpiStore;
+    if (!on(kCatGemm)) return rope_cos && epi == kEpiStore;
     CUtensorMap xmap = make_map(e->x4, M, w.K / 2, 1, bn);
     GemmParams p{};
     p.M = M;
@@ -419,7 +446,7 @@ struct Fwd {
       p.tma_epilogue = output_map(&omap, p, bn);
       if (!p.tma_epilogue) fail("output tensor map rejected for a %dx%d projection", M, w.N);
     }
-    const bool rotated = p.tma_epilogue && rope_cos && epi == kEpiStore;
+    const bool rotated = rope_cos && epi == kEpiStore;
     if (rotated) {
       p.rope_cos = rope_cos;
       p.rope_sin = rope_sin;
@@ -503,40 +530,41 @@ struct Fwd {
       const bool glob = (i % c.global_every) == 0;
       const float* rc = glob ? E.gcos : E.lcos;
       const float* rs = glob ? E.gsin : E.lsin;
-      // The rotary embedding runs in the projection's epilogue when it uses
-      // the wide (unsplit, 128-token) epilogue, else in the attention kernel.
+      // The rotary embedding runs in the projection's epilogue.
       const bool rotated =
           nv4 ? gemm_nv4(E.wqkv[i], E.n, T, kEpiStore, E.qkv, 3 * d, nullptr, 0, rc, rs, s)
               : gemm(E.wqkv[i], fp8 ? (const void*)E.n8 : (const void*)E.n, E.n8s, T, kEpiStore, E.qkv, 3 * d,
                      nullptr, 0, rc, rs, s);
-      {
-        AttnParams a{};
-        a.qkv = E.qkv;
-        a.ld_qkv = 3 * d;
-        a.d = d;
-        a.s = s;
-        a.nq = s;
-        a.key_valid = valid;
-        a.cos = rotated ? nullptr : rc;
-        a.sin = rotated ? nullptr : rs;
-        a.window = glob ? -1 : c.local_window;
-        a.out = E.attn;
-        a.ld_out = d;
+      AttnParams a{};
+      a.qkv = E.qkv;
+      a.ld_qkv = 3 * d;
+      a.d = d;
+      a.s = s;
+      a.nq = s;
+      a.key_valid = valid;
+      a.cos = rotated ? nullptr : rc;
+      a.sin = rotated ? nullptr : rs;
+      a.window = glob ? -1 : c.local_window;
+      a.out = E.attn;
+      a.ld_out = d;
+      // One short sequence in bf16: attention inside the Wo projection.
+      const bool fused = !fp8 && !nv4 && b == 1 && gemm_attn(E.wo[i], a, T);
+      if (!fused) {
         attention(a, b, c.heads);
+        if (fp8 && on(kCatQuant)) {
+          QuantParams q{};
+          q.rows = T;
+          q.k = d;
+          q.src = E.attn;
+          q.q = E.a8;
+          q.scale = E.a8s;
+          count(launch_quant_fp8(q, st, pdl()), "quant launch");
+        }
+        if (nv4)
+          gemm_nv4(E.wo[i], E.attn, T, kEpiResidual, nullptr, 0, E.h, d);
+        else
+          gemm(E.wo[i], fp8 ? (const void*)E.a8 : (const void*)E.attn, E.a8s, T, kEpiResidual, nullptr, 0, E.h, d);
       }
-      if (fp8 && on(kCatQuant)) {
-        QuantParams q{};
-        q.rows = T;
-        q.k = d;
-        q.src = E.attn;
-        q.q = E.a8;
-        q.scale = E.a8s;
-        count(launch_quant_fp8(q, st, pdl()), "quant launch");
-      }
-      if (nv4)
-        gemm_nv4(E.wo[i], E.attn, T, kEpiResidual, nullptr, 0, E.h, d);
-      else
-        gemm(E.wo[i], fp8 ? (const void*)E.a8 : (const void*)E.attn, E.a8s, T, kEpiResidual, nullptr, 0, E.h, d);
       {
         NormParams p{};
         p.rows = T;

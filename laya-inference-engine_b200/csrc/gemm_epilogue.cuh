@@ -83,6 +83,62 @@ DEVI void epilogue_quad(const GemmParams& p, int m, int n_lo, int geglu_col, flo
   *reinterpret_cast<uint2*>(o + n_hi) = *reinterpret_cast<uint2*>(oh);
 }
 
+// Rotary epilogue (plain store) for rows n_lo..n_lo+3 of a q or k head
+// (n_lo & 63 < 32) and their rotation partners n_lo+32..n_lo+35 of token m:
+// bf16(qkv) rotated in fp32 without FMA contraction, as rope_qkv does
+// (kernels.py:62-93), at the token's position m % rope_seq.
+template <int KIND>
+DEVI void epilogue_rope(const GemmParams& p, int m, int n_lo, float4 lo, float4 hi) {
+  float l[4] = {lo.x, lo.y, lo.z, lo.w}, h[4] = {hi.x, hi.y, hi.z, hi.w};
+  const int n_hi = n_lo + 32;
+  if (KIND == kKindFp8) {
+    const float sa = p.a_scale[m];
+    const float4 wl = *reinterpret_cast<const float4*>(p.w_scale + n_lo);
+    const float4 wh = *reinterpret_cast<const float4*>(p.w_scale + n_hi);
+    const float wlv[4] = {wl.x, wl.y, wl.z, wl.w}, whv[4] = {wh.x, wh.y, wh.z, wh.w};
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      l[e] = (l[e] * sa) * wlv[e];
+      h[e] = (h[e] * sa) * whv[e];
+    }
+  } else if (KIND == kKindNvfp4) {
+    const float sa = p.a_scale[m] * p.w_tensor_scale;
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      l[e] *= sa;
+      h[e] *= sa;
+    }
+  }
+  if (p.bias) {
+    const uint2 bl = *reinterpret_cast<const uint2*>(p.bias + n_lo);
+    const uint2 bh = *reinterpret_cast<const uint2*>(p.bias + n_hi);
+    const __nv_bfloat16* bla = reinterpret_cast<const __nv_bfloat16*>(&bl);
+    const __nv_bfloat16* bha = reinterpret_cast<const __nv_bfloat16*>(&bh);
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      l[e] += __bfloat162float(bla[e]);
+      h[e] += __bfloat162float(bha[e]);
+    }
+  }
+  const int pos = m % p.rope_seq, d0 = n_lo & 63;
+  const float4 c0 = *reinterpret_cast<const float4*>(p.rope_cos + (size_t)pos * 64 + d0);
+  const float4 c1 = *reinterpret_cast<const float4*>(p.rope_cos + (size_t)pos * 64 + d0 + 32);
+  const float4 s0 = *reinterpret_cast<const float4*>(p.rope_sin + (size_t)pos * 64 + d0);
+  const float4 s1 = *reinterpret_cast<const float4*>(p.rope_sin + (size_t)pos * 64 + d0 + 32);
+  const float cl[4] = {c0.x, c0.y, c0.z, c0.w}, ch[4] = {c1.x, c1.y, c1.z, c1.w};
+  const float sl[4] = {s0.x, s0.y, s0.z, s0.w}, sh[4] = {s1.x, s1.y, s1.z, s1.w};
+  __nv_bfloat16 ol[4], oh[4];
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+    const float a = bf16_round(l[e]), b = bf16_round(h[e]);
+    ol[e] = __float2bfloat16_rn(__fadd_rn(__fmul_rn(a, cl[e]), __fmul_rn(-b, sl[e])));
+    oh[e] = __float2bfloat16_rn(__fadd_rn(__fmul_rn(b, ch[e]), __fmul_rn(a, sh[e])));
+  }
+  __nv_bfloat16* o = p.out + (size_t)m * p.ldo;
+  *reinterpret_cast<uint2*>(o + n_lo) = *reinterpret_cast<uint2*>(ol);
+  *reinterpret_cast<uint2*>(o + n_hi) = *reinterpret_cast<uint2*>(oh);
+}
+
 // TMEM accumulator -> shared partial -> cluster reduction -> epilogue.
 // Called by all 128 threads after the MMA-done barrier completed.
 // `part` is this CTA's shared scratch of at least BN*128 floats (the
@@ -124,19 +180,22 @@ DEVI void tile_epilogue(const GemmParams& p, uint32_t tmem, float* part, int til
     __syncthreads();
 
   // ---- reduction over the cluster and the epilogue: a thread takes 4
-  // consecutive rows (and their +64 partners) of one token and sums the S
+  // consecutive rows of one token and their partners (+64: the GEGLU gate;
+  // +32 in the rotary tiles of q and k: the rotation partner) and sums the S
   // partials in rank order with 16-byte loads issued back to back.
   const uint32_t part_addr = smem_u32(part);
+  const bool rope = tile_n * 128 < p.rope_cols;
+  const int pair = rope ? 32 : 64;
   for (int item = tid; tid < 128 && item < nt * 16; item += 128) {
     const int tl = t0 + (item >> 4);
-    const int q4 = (item & 15) * 4;
+    const int q4 = rope ? ((item >> 3) & 1) * 64 + (item & 7) * 4 : (item & 15) * 4;
     const int m = tile_m * BN + tl;
     if (m >= p.M) continue;
     const int off = tl * 128 + q4;
     float4 lo, hi;
     if (split == 1) {
       lo = *reinterpret_cast<const float4*>(part + off);
-      hi = *reinterpret_cast<const float4*>(part + off + 64);
+      hi = *reinterpret_cast<const float4*>(part + off + pair);
     } else {
       lo = make_float4(0.f, 0.f, 0.f, 0.f);
       hi = lo;
@@ -149,11 +208,11 @@ DEVI void tile_epilogue(const GemmParams& p, uint32_t tmem, float* part, int til
             if (gpath) {  // L2 loads (the cluster barrier ordered the peers' stores)
               const float* src = p.partials + ((size_t)(tile_m * gridDim.x + tile_n) * split + q0 + u) * BN * 128 + off;
               va[u] = __ldcg(reinterpret_cast<const float4*>(src));
-              vb[u] = __ldcg(reinterpret_cast<const float4*>(src + 64));
+              vb[u] = __ldcg(reinterpret_cast<const float4*>(src + pair));
             } else {
               const uint32_t base = mapa_shared(part_addr, (uint32_t)(q0 + u));
               va[u] = ld_dsmem_f32x4(base + off * 4);
-              vb[u] = ld_dsmem_f32x4(base + (off + 64) * 4);
+              vb[u] = ld_dsmem_f32x4(base + (off + pair) * 4);
             }
           }
 #pragma unroll
@@ -164,7 +223,10 @@ DEVI void tile_epilogue(const GemmParams& p, uint32_t tmem, float* part, int til
           }
       }
     }
-    epilogue_quad<KIND>(p, m, tile_n * 128 + q4, tile_n * 64 + q4, lo, hi);
+    if (rope)
+      epilogue_rope<KIND>(p, m, tile_n * 128 + q4, lo, hi);
+    else
+      epilogue_quad<KIND>(p, m, tile_n * 128 + q4, tile_n * 64 + q4, lo, hi);
   }
   if (split > 1 && !gpath) cluster_sync_all();
 

@@ -13,6 +13,12 @@ int gemm_k_elems(int kind);
 int gemm_split(int tiles, int kblocks, int sm_count, int max_split);
 cudaError_t launch_gemm(int kind, const CUtensorMap& wmap, const CUtensorMap& xmap, const CUtensorMap& omap,
                         const GemmParams& p, int bn, int split, cudaStream_t stream, bool pdl);
+
+// Fused attention + residual output projection for one sequence of
+// 32 < s <= 64 tokens (bf16, q and k already rotated): attention of the CTA's
+// heads computed in shared memory as the B operand (gemm_attn.cu).
+cudaError_t launch_gemm_attn(const CUtensorMap& wmap, const GemmParams& p, const AttnParams& a, int split,
+                             cudaStream_t stream, bool pdl);
 cudaError_t launch_gemm_nvfp4(const CUtensorMap& wmap, const CUtensorMap& xmap, const CUtensorMap& omap,
                               const uint8_t* wsf,
                               const uint8_t* xsf, int sf_kbs, const GemmParams& p, int bn, int split,
