@@ -94,8 +94,10 @@ LAYA_B200_API int laya_b200_kernel_count(laya_b200_engine* e, int slot, int* cou
 /* Test hook with no counterpart in the reference: copy the first `bytes` of
  * a named activation buffer ("h", "n", "qkv", "attn", "g", "hsel", "msc",
  * "zsc"; with FP8 also the e4m3 codes and per-row scales "n8", "n8s", "a8",
- * "a8s", "g8", "g8s") to host memory after synchronising, so kernel-level
- * tests can compare intermediate results with a CPU oracle. */
+ * "a8s", "g8", "g8s"; with NVFP4 the last quantised operand "x4" (e2m1
+ * nibbles), "x4sf" (e4m3 block scales, tiled) and "x4o" (per-row outer
+ * scales)) to host memory after synchronising, so kernel-level tests can
+ * compare intermediate results with a CPU oracle. */
 LAYA_B200_API int laya_b200_read_buffer(laya_b200_engine* e, const char* name, void* dst, size_t bytes);
 
 /* Arguments of laya_b200_tail_noalloc: device pointers the caller owns. */

@@ -936,7 +936,8 @@ int laya_b200_finalize(laya_b200_engine* e, int precision) {
     const laya_b200_config& c = e->cfg;
     const int kind = precision == LAYA_B200_FP8 ? kKindFp8 : precision == LAYA_B200_NVFP4 ? kKindNvfp4 : kKindBf16;
     if (kind == kKindNvfp4 && (c.hidden % 16 || c.intermediate % 16)) fail("NVFP4 needs K divisible by 16");
-    if (kind == kKindFp8 && c.intermediate > 4096) fail("FP8 needs intermediate <= 4096 (row quantiser width)");
+    if (kind != kKindBf16 && c.intermediate > 4096)
+      fail("FP8 and NVFP4 need intermediate <= 4096 (row quantiser width)");
     std::vector<std::pair<std::string, size_t>> qoff;  // weight name -> offset of e4m3 bytes, scales follow
     if (kind == kKindFp8) {
       size_t off = 0;
@@ -1174,6 +1175,12 @@ int laya_b200_read_buffer(laya_b200_engine* e, const char* name, void* dst, size
     else if (n == "a8s" && e->a8s) { src = e->a8s; cap = T * 4; }
     else if (n == "g8" && e->g8) { src = e->g8; cap = T * (size_t)c.intermediate; }
     else if (n == "g8s" && e->g8s) { src = e->g8s; cap = T * 4; }
+    else if (n == "x4" && e->x4) { src = e->x4; cap = T * (size_t)std::max(d, (size_t)c.intermediate) / 2; }
+    else if (n == "x4sf" && e->x4sf) {
+      src = e->x4sf;
+      cap = ((T + 15) / 16) * (size_t)(4 * ((std::max(d, (size_t)c.intermediate) + 255) / 256)) * 512;
+    }
+    else if (n == "x4o" && e->x4o) { src = e->x4o; cap = T * 4; }
     else fail("unknown buffer %s", name);
     if (bytes > cap) fail("buffer %s holds %zu bytes, %zu requested", name, cap, bytes);
     ck(cudaStreamSynchronize(e->stream), "sync");

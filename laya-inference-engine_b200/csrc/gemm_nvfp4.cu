@@ -273,14 +273,61 @@ __global__ void __launch_bounds__(256) nvfp4_pack_weight_kernel(const __nv_bfloa
   nvfp4_row(w + (size_t)row * k, k, outer, nullptr, q + (size_t)row * (k / 2), sf, row, 128, col_blocks, lane);
 }
 
+// Activation quantiser: one warp per row (k <= 256*MAXC), the same values as
+// nvfp4_row with a per-row outer scale.  The row is loaded into registers with
+// every load in flight at once; lane l holds elements [8l + 256i, +8), so a
+// 16-element block is split over a lane pair and its maximum takes one
+// shuffle; quotients use the FMA-corrected division (correctly rounded).
+template <int MAXC>
 __global__ void __launch_bounds__(256) quant_nvfp4_kernel(const QuantParams p, int rows_per_block, int col_blocks) {
   griddep_launch_dependents();
   griddep_wait();
   const int lane = threadIdx.x & 31;
   const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   if (row >= p.rows) return;
-  nvfp4_row(p.src + (size_t)row * p.k, p.k, 0.f, p.scale + row, p.q + (size_t)row * (p.k / 2), p.sf, row,
-            rows_per_block, col_blocks, lane);
+  const __nv_bfloat16* src = p.src + (size_t)row * p.k;
+  uint4 u[MAXC];
+#pragma unroll
+  for (int i = 0; i < MAXC; ++i) {
+    const int c = lane * 8 + 256 * i;
+    u[i] = c < p.k ? *reinterpret_cast<const uint4*>(src + c) : make_uint4(0, 0, 0, 0);
+  }
+  float amax = 0.f;
+#pragma unroll
+  for (int i = 0; i < MAXC; ++i) {
+    const __nv_bfloat16* e = reinterpret_cast<const __nv_bfloat16*>(&u[i]);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) amax = fmaxf(amax, fabsf(__bfloat162float(e[j])));
+  }
+  amax = warp_max(amax);
+  const float outer = fmaxf(amax / (6.0f * 448.0f), 1e-20f);
+  if (lane == 0) p.scale[row] = outer;
+  const float o6 = 6.0f * outer, inv_o6 = 1.0f / o6;
+  uint8_t* q = p.q + (size_t)row * (p.k / 2);
+#pragma unroll
+  for (int i = 0; i < MAXC; ++i) {
+    const int c = lane * 8 + 256 * i;
+    const __nv_bfloat16* e = reinterpret_cast<const __nv_bfloat16*>(&u[i]);
+    float x[8], bmax = 0.f;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      x[j] = __bfloat162float(e[j]);
+      bmax = fmaxf(bmax, fabsf(x[j]));
+    }
+    bmax = fmaxf(bmax, __shfl_xor_sync(0xffffffffu, bmax, 1));  // the lane pair of one 16-element block
+    if (c >= p.k) continue;
+    const float sc = fmaxf(div_rn_by(bmax, o6, inv_o6), 0.001953125f);  // 2^-9 floor
+    const uint8_t sc8 = (uint8_t)(f32x2_to_e4m3x2(sc, 0.f) & 0xFF);
+    const int ex = (sc8 >> 3) & 0xF, mt = sc8 & 7;
+    const float scale = ex == 0 ? ldexpf((float)mt, -9) : ldexpf(1.0f + mt / 8.0f, ex - 7);
+    const float denom = scale * outer, inv_d = 1.0f / denom;
+    uint32_t w = 0;
+#pragma unroll
+    for (int j = 0; j < 8; j += 2)
+      w |= (uint32_t)f32x2_to_e2m1x2(div_rn_by(x[j], denom, inv_d), div_rn_by(x[j + 1], denom, inv_d)) << (4 * j);
+    *reinterpret_cast<uint32_t*>(q + c / 2) = w;
+    if ((lane & 1) == 0) p.sf[sf_offset(row, c / 16, rows_per_block, col_blocks)] = sc8;
+  }
 }
 
 // ------------------------------------------------------------- host side
@@ -360,9 +407,13 @@ cudaError_t launch_nvfp4_pack_weight(const __nv_bfloat16* w, int rows, int k, un
 
 cudaError_t launch_quant_nvfp4(const QuantParams& p, int rows_per_block, int col_blocks, cudaStream_t stream,
                                bool pdl) {
-  if (p.k % 16) return cudaErrorInvalidValue;
+  if (p.k % 16 || p.k > 4096) return cudaErrorInvalidValue;
   QuantParams q = p;
   void* args[] = {&q, &rows_per_block, &col_blocks};
+  const void* kern = p.k <= 1024   ? (const void*)quant_nvfp4_kernel<4>
+                     : p.k <= 2048 ? (const void*)quant_nvfp4_kernel<8>
+                     : p.k <= 3072 ? (const void*)quant_nvfp4_kernel<12>
+                                   : (const void*)quant_nvfp4_kernel<16>;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((p.rows + 7) / 8, 1, 1);
   cfg.blockDim = dim3(256, 1, 1);
@@ -372,7 +423,7 @@ cudaError_t launch_quant_nvfp4(const QuantParams& p, int rows_per_block, int col
   attr.val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = &attr;
   cfg.numAttrs = pdl ? 1 : 0;
-  return cudaLaunchKernelExC(&cfg, (const void*)quant_nvfp4_kernel, args);
+  return cudaLaunchKernelExC(&cfg, kern, args);
 }
 
 }  // namespace laya

@@ -210,3 +210,46 @@ def test_fused_attention_projection_matches_oracle(s, length):
         assert nf.kernel_count(slot) == nf.kernel_count(two) - cfg.layers
     finally:
         nf.close()
+
+
+def _sf_offset(row, g, rows_per_block, col_blocks):
+    rb, r = row // rows_per_block, row % rows_per_block
+    return (rb * col_blocks + (g >> 2)) * 512 + (r & 31) * 16 + (r >> 5) * 4 + (g & 3)
+
+
+@pytest.mark.parametrize("intermediate", [384, 1920, 2624, 4096])
+def test_nvfp4_activation_quantiser_is_bit_exact(intermediate):
+    """The per-row NVFP4 activation quantiser (nvfp4.py:36-51 with a per-row
+    outer scale) on the GEGLU output against the oracle's restatement: outer
+    scales, e4m3 block scales and e2m1 codes identical."""
+    from laya_b200.engine import NativeForward
+    cfg = LayaConfig(layers=1, hidden=256, heads=4, intermediate=intermediate, vocab=1000, pad_token_id=999,
+                     max_len=512, head_layers=0, head_heads=4, head_ff=512, act_hidden=64)
+    w = seeded_weights(cfg, seed=6)
+    nf = NativeForward(0, cfg, w, "nvfp4", max_batch=4, max_options=8)
+    try:
+        b, s, k = 2, 192, 4
+        items = synthetic_items([192, 100], ["choice", "noul"], seed=13, vocab=cfg.vocab)
+        nf.run(nf.capture(b, s, k, False), pack(items, b, s, k, cfg.pad_token_id))
+        T, K = b * s, intermediate
+        col_blocks = 4 * ((K + 255) // 256)
+        rows_per_block = 128  # token tile of the Wo2 projection at 384 tokens
+        x = bf16_of(nf.read_buffer("g", (T, K), np.uint16))
+        nib = nf.read_buffer("x4", (T, K // 2), np.uint8)
+        sf_bytes = ((T + rows_per_block - 1) // rows_per_block) * col_blocks * 512
+        sf = nf.read_buffer("x4sf", (sf_bytes,), np.uint8)
+        outer = torch.from_numpy(nf.read_buffer("x4o", (T,), np.float32))
+    finally:
+        nf.close()
+    ref_deq, ref_outer = O.nvfp4_quantize(x, per_row=True)
+    assert torch.equal(outer, ref_outer[:, 0])
+    rows = np.arange(T)[:, None]
+    groups = np.arange(K // 16)[None, :]
+    idx = _sf_offset(rows, groups, rows_per_block, col_blocks)
+    scale = torch.from_numpy(sf[idx].copy()).view(torch.float8_e4m3fn).to(torch.float32)  # [T, K/16]
+    codes = np.stack([nib & 0xF, nib >> 4], axis=-1).reshape(T, K)
+    grid = np.array([0.0, 0.5, 1.0, 1.5, 2.0, 3.0, 4.0, 6.0], np.float32)
+    vals = grid[codes & 7] * np.where(codes & 8, -1.0, 1.0).astype(np.float32)
+    deq = torch.from_numpy(vals).view(T, K // 16, 16) * scale[:, :, None]
+    ref = ref_deq.view(T, K // 16, 16)
+    assert torch.equal(deq, ref), int((deq != ref).sum())
