@@ -16,6 +16,7 @@
 #include <cstdarg>
 #include <cstdio>
 #include <algorithm>
+#include <cstdlib>
 #include <cstring>
 #include <functional>
 #include <map>
@@ -224,6 +225,10 @@ struct laya_b200_engine {
 
   std::vector<Slot> slots;
   int launches = 0;  // counter while enqueuing
+  // Diagnostic mode (environment LAYA_B200_SYNC_CHECK=1 at create): run()
+  // enqueues the forward without a graph and synchronises after every
+  // launch, so a device error names the launch that raised it.
+  bool sync_check = false;
 
   std::vector<cudaEvent_t> timing_events;
 };
@@ -318,6 +323,7 @@ struct Fwd {
   cudaStream_t st;
   int mask = kCatAll;  // enqueue only kernels of these categories
   bool first = true;
+  bool eager_check = false;  // synchronise and check after every launch
 
   bool on(int cat) const { return (mask & cat) != 0; }
   bool pdl() {
@@ -329,6 +335,10 @@ struct Fwd {
     ck(err, what);
     ck(cudaGetLastError(), what);
     e->launches++;
+    if (eager_check) {
+      const cudaError_t r = cudaStreamSynchronize(st);
+      if (r != cudaSuccess) fail("launch %d (%s): %s", e->launches, what, cudaGetErrorString(r));
+    }
   }
 
   // Returns true when the epilogue applied the rotary embedding (cos / sin
@@ -511,22 +521,44 @@ struct Fwd {
       }
       norm(p);
     }
+    // LayerNorm feeding an encoder projection: bf16, or e4m3 + row scales.
+    auto enc_norm = [&](const std::string& wname) {
+      NormParams p{};
+      p.rows = T;
+      p.src = E.h;
+      p.ld_src = d;
+      p.w = wptr<float>(e, wname);
+      if (fp8) {
+        p.out_fp8 = E.n8;
+        p.out_fp8_scale = E.n8s;
+      } else {
+        p.out_bf16 = E.n;
+      }
+      return p;
+    };
+    // final_norm(h + pending) + type_emb(qtype) (model.py:102-104), fused with
+    // the first head layer's norm1 (model.py:59).
+    NormParams final_norm{};
+    final_norm.rows = T;
+    final_norm.src = E.h;
+    final_norm.ld_src = d;
+    final_norm.w = wptr<float>(e, "final_norm.w");
+    final_norm.add_table = wptr<float>(e, "type_emb");
+    final_norm.add_idx = qtype;
+    final_norm.add_div = s;
+    final_norm.out_f32 = E.h;
+    final_norm.ld_out_f32 = d;
+    if (c.head_layers > 0) {
+      final_norm.second_w = wptr<float>(e, "head.0.norm1.w");
+      final_norm.second_b = wptr<float>(e, "head.0.norm1.b");
+      final_norm.out_bf16 = E.n;
+    }
+    if (c.layers == 0) norm(final_norm);
+    // Each residual projection (Wo, Wo2) is followed by add_norm
+    // (model.py:15-19): mlp_norm after Wo, the next layer's attn_norm (or the
+    // final norm) after Wo2.
     for (int i = 0; i < c.layers; ++i) {
       const std::string pre = "enc." + std::to_string(i) + ".";
-      if (i > 0) {  // add_norm(h, pending, attn_norm): pending already added by Wo2's epilogue
-        NormParams p{};
-        p.rows = T;
-        p.src = E.h;
-        p.ld_src = d;
-        p.w = wptr<float>(e, pre + "attn_norm.w");
-        if (fp8) {
-          p.out_fp8 = E.n8;
-          p.out_fp8_scale = E.n8s;
-        } else {
-          p.out_bf16 = E.n;
-        }
-        norm(p);
-      }
       const bool glob = (i % c.global_every) == 0;
       const float* rc = glob ? E.gcos : E.lcos;
       const float* rs = glob ? E.gsin : E.lsin;
@@ -565,20 +597,7 @@ struct Fwd {
         else
           gemm(E.wo[i], fp8 ? (const void*)E.a8 : (const void*)E.attn, E.a8s, T, kEpiResidual, nullptr, 0, E.h, d);
       }
-      {
-        NormParams p{};
-        p.rows = T;
-        p.src = E.h;
-        p.ld_src = d;
-        p.w = wptr<float>(e, pre + "mlp_norm.w");
-        if (fp8) {
-          p.out_fp8 = E.n8;
-          p.out_fp8_scale = E.n8s;
-        } else {
-          p.out_bf16 = E.n;
-        }
-        norm(p);
-      }
+      norm(enc_norm(pre + "mlp_norm.w"));
       if (nv4)
         gemm_nv4(E.wi[i], E.n, T, kEpiGeglu, E.g, I, nullptr, 0);
       else
@@ -596,40 +615,14 @@ struct Fwd {
         gemm_nv4(E.wo2[i], E.g, T, kEpiResidual, nullptr, 0, E.h, d);
       else
         gemm(E.wo2[i], fp8 ? (const void*)E.g8 : (const void*)E.g, E.g8s, T, kEpiResidual, nullptr, 0, E.h, d);
+      // add_norm after Wo2: the next layer's attn_norm, or the final norm
+      norm(i + 1 < c.layers ? enc_norm("enc." + std::to_string(i + 1) + ".attn_norm.w") : final_norm);
     }
-    // final_norm(h + pending) + type_emb(qtype) (model.py:102-104), fused with
-    // the first head layer's norm1 (model.py:59).
-    {
-      NormParams p{};
-      p.rows = T;
-      p.src = E.h;
-      p.ld_src = d;
-      p.w = wptr<float>(e, "final_norm.w");
-      p.add_table = wptr<float>(e, "type_emb");
-      p.add_idx = qtype;
-      p.add_div = s;
-      p.out_f32 = E.h;
-      p.ld_out_f32 = d;
-      if (c.head_layers > 0) {
-        p.second_w = wptr<float>(e, "head.0.norm1.w");
-        p.second_b = wptr<float>(e, "head.0.norm1.b");
-        p.out_bf16 = E.n;
-      }
-      norm(p);
-    }
+    // Head layers (model.py:58-70): norm1 of layer j > 0 follows the previous
+    // layer's linear2, norm2 follows out_proj.
     for (int j = 0; j < c.head_layers; ++j) {
       const std::string pre = "head." + std::to_string(j) + ".";
       const bool last = j == c.head_layers - 1;
-      if (j > 0) {
-        NormParams p{};
-        p.rows = T;
-        p.src = E.h;
-        p.ld_src = d;
-        p.w = wptr<float>(e, pre + "norm1.w");
-        p.b = wptr<float>(e, pre + "norm1.b");
-        p.out_bf16 = E.n;
-        norm(p);
-      }
       gemm(E.in_proj[j], E.n, nullptr, T, kEpiStore, E.qkv, 3 * d, nullptr, 0);
       AttnParams a{};
       a.qkv = E.qkv;
@@ -660,19 +653,30 @@ struct Fwd {
         nrows = E.nsel;
         frows = E.fsel;
       }
+      NormParams norm2{};
+      norm2.rows = rows;
+      norm2.src = hrows;
+      norm2.ld_src = d;
+      norm2.w = wptr<float>(e, pre + "norm2.w");
+      norm2.b = wptr<float>(e, pre + "norm2.b");
+      norm2.out_bf16 = nrows;
       gemm(E.out_proj[j], arows, nullptr, rows, kEpiResidual, nullptr, 0, hrows, d);
-      {
-        NormParams p{};
-        p.rows = rows;
-        p.src = hrows;
-        p.ld_src = d;
-        p.w = wptr<float>(e, pre + "norm2.w");
-        p.b = wptr<float>(e, pre + "norm2.b");
-        p.out_bf16 = nrows;
-        norm(p);
-      }
+      norm(norm2);
       gemm(E.lin1[j], nrows, nullptr, rows, kEpiRelu, frows, F, nullptr, 0);
-      gemm(E.lin2[j], frows, nullptr, rows, kEpiResidual, nullptr, 0, hrows, d);
+      if (last) {
+        gemm(E.lin2[j], frows, nullptr, rows, kEpiResidual, nullptr, 0, hrows, d);
+      } else {  // norm1 of the next layer, on the same T rows
+        const std::string nxt = "head." + std::to_string(j + 1) + ".";
+        NormParams norm1{};
+        norm1.rows = T;
+        norm1.src = E.h;
+        norm1.ld_src = d;
+        norm1.w = wptr<float>(e, nxt + "norm1.w");
+        norm1.b = wptr<float>(e, nxt + "norm1.b");
+        norm1.out_bf16 = E.n;
+        gemm(E.lin2[j], frows, nullptr, rows, kEpiResidual, nullptr, 0, hrows, d);
+        norm(norm1);
+      }
     }
     if (c.head_layers == 0 && on(kCatRows))
       count(launch_gather_rows(E.hsel, E.h, selsrc, R, d, st, pdl()), "gather launch");
@@ -809,6 +813,10 @@ int laya_b200_create(int device, const laya_b200_config* cfg, laya_b200_engine**
     ck(cudaGetDeviceProperties(&prop, device), "cudaGetDeviceProperties");
     if (prop.major != 10) fail("the b200 engine needs an sm_100 GPU; found %s (SM%d%d)", prop.name, prop.major, prop.minor);
     e->sm_count = prop.multiProcessorCount;
+    {
+      const char* v = getenv("LAYA_B200_SYNC_CHECK");
+      e->sync_check = v && v[0] == '1';
+    }
     ck(cudaStreamCreateWithFlags(&e->stream, cudaStreamNonBlocking), "stream");
     ck(cudaEventCreate(&e->ev0), "event");
     ck(cudaEventCreate(&e->ev1), "event");
@@ -1107,7 +1115,16 @@ int laya_b200_run(laya_b200_engine* e, int slot, const int64_t* input_ids, const
         w[L.score + q * k + j] = q * (1 + k) + 1 + j;
       }
     }
-    ck(cudaGraphLaunch(sl.io_exec, e->stream), "graph launch");
+    if (e->sync_check) {
+      ck(cudaMemcpyAsync(e->d_in, e->h_in, L.words * 4, cudaMemcpyHostToDevice, e->stream), "H2D");
+      e->launches = 0;
+      Fwd f{e, e->stream, kCatAll};
+      f.eager_check = true;
+      f.run(sl.sh);
+      ck(cudaMemcpyAsync(e->h_out, e->d_out, L.out_words * 4, cudaMemcpyDeviceToHost, e->stream), "D2H");
+    } else {
+      ck(cudaGraphLaunch(sl.io_exec, e->stream), "graph launch");
+    }
     ck(cudaStreamSynchronize(e->stream), "forward");
     const uint32_t st = __atomic_load_n(e->status_host, __ATOMIC_ACQUIRE);
     if (st) {

@@ -17,6 +17,33 @@ enum GemmEpilogue : int {
 
 enum GemmKind : int { kKindBf16 = 0, kKindFp8 = 1, kKindNvfp4 = 2 };
 
+struct NormParams {
+  int rows;
+  int d;
+  float eps;
+  // Source rows: embedding table gathered by token id, or an fp32 matrix
+  // (optionally through a row map).
+  const int* tok_ids;       // [rows] or null
+  const float* src;         // fp32 [*, ld_src] (table when tok_ids != null)
+  int ld_src;
+  const int* row_map;       // [rows] source row per output row, or null
+  const float* w;           // LayerNorm weight [d]
+  const float* b;           // LayerNorm bias [d] or null
+  // y = LN(x) * w + b (+ add_table[add_idx[row / add_div]])
+  const float* add_table;   // [*, d] or null
+  const int* add_idx;
+  int add_div;
+  float* out_f32;           // y (fp32) or null; may alias src (in place)
+  int ld_out_f32;
+  // bf16 output: bf16(y) when second_w == null; otherwise bf16(LN2(y)) with
+  // second_w / second_b (a second LayerNorm fused on the same row).
+  const float* second_w;
+  const float* second_b;
+  __nv_bfloat16* out_bf16;  // [rows][d] or null
+  uint8_t* out_fp8;         // e4m3 per-row quantisation of the bf16 output, or null
+  float* out_fp8_scale;     // [rows]
+};
+
 struct GemmParams {
   int M;          // token rows
   int N;          // weight rows (features) -- multiple of 128
@@ -46,33 +73,6 @@ struct GemmParams {
   float* partials;           // global split-K partials [tiles][split][BN][128] floats, or null
 };
 
-struct NormParams {
-  int rows;
-  int d;
-  float eps;
-  // Source rows: embedding table gathered by token id, or an fp32 matrix
-  // (optionally through a row map).
-  const int* tok_ids;       // [rows] or null
-  const float* src;         // fp32 [*, ld_src] (table when tok_ids != null)
-  int ld_src;
-  const int* row_map;       // [rows] source row per output row, or null
-  const float* w;           // LayerNorm weight [d]
-  const float* b;           // LayerNorm bias [d] or null
-  // y = LN(x) * w + b (+ add_table[add_idx[row / add_div]])
-  const float* add_table;   // [*, d] or null
-  const int* add_idx;
-  int add_div;
-  float* out_f32;           // y (fp32) or null; may alias src (in place)
-  int ld_out_f32;
-  // bf16 output: bf16(y) when second_w == null; otherwise bf16(LN2(y)) with
-  // second_w / second_b (a second LayerNorm fused on the same row).
-  const float* second_w;
-  const float* second_b;
-  int raw_bf16;             // 1: bf16 output is bf16(x) of the *input* row (encoder layer 0 input)
-  __nv_bfloat16* out_bf16;  // [rows][d] or null
-  uint8_t* out_fp8;         // e4m3 per-row quantisation of the bf16 output, or null
-  float* out_fp8_scale;     // [rows]
-};
 
 struct AttnParams {
   const __nv_bfloat16* qkv;  // [tokens][ld_qkv]; q at col h*64, k at d + h*64, v at 2d + h*64
