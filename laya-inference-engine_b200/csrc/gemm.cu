@@ -49,6 +49,9 @@ __global__ void __launch_bounds__(BN >= 128 ? 256 : 128, BN == 128 ? 2 : 1)
     gemm_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ CUtensorMap xmap,
                 const __grid_constant__ CUtensorMap omap, const GemmParams p) {
   using C = GemmCfg<BN, KIND, STAGES>;
+  // All shared memory of the projection kernels is this dynamic block (a
+  // static __shared__ variable in the epilogue made the TMA-store epilogue
+  // fault with an illegal address; the cause was not established).
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;
