@@ -207,6 +207,7 @@ struct laya_b200_engine {
   float* x4o = nullptr;             // nvfp4 per-row outer scales [T]
   int x4_col_blocks = 0;
   float* gpart = nullptr;           // split-K partials of the cluster reduction (kPartialFloats)
+  float2* lnst = nullptr;           // LayerNorm tile statistics [T][hidden/128] (batch-1 path)
   float* a1 = nullptr;              // tail scratch [max_batch][act_hidden]
   unsigned int* arrivals = nullptr; // tail arrival counters [max_batch]
   // device inputs / outputs (int32 staging layout)
@@ -345,7 +346,7 @@ struct Fwd {
   // given, plain store) to the output's q and k columns.
   bool gemm(const Proj& w, const void* x, const float* x_scale, int M, int epi, __nv_bfloat16* out, int ldo,
             float* resid, int ldr, const float* rope_cos = nullptr, const float* rope_sin = nullptr,
-            int rope_seq = 0) {
+            int rope_seq = 0, bool ln_stats = false) {
     const int kb = (w.K + gemm_k_elems(w.kind) - 1) / gemm_k_elems(w.kind);
     int bn = 0, split = 1;
     gemm_plan(M, w.N, kb, e->sm_count, &bn, &split);
@@ -381,6 +382,7 @@ struct Fwd {
       p.rope_seq = rope_seq;
       p.rope_cols = 2 * (w.N / 3);
     }
+    if (ln_stats) p.ln_stats = e->lnst;
     count(launch_gemm(w.kind, w.map, xmap, omap, p, bn, split, st, pdl()), "gemm launch");
     return rotated;
   }
@@ -408,8 +410,61 @@ struct Fwd {
     p.bias = w.bias;
     p.status = e->status_dev;
     if (split > 1 && (size_t)(w.N / 128) * split * bn * 128 <= kPartialFloats) p.partials = e->gpart;
+    p.ln_stats = e->lnst;
     count(launch_gemm_attn(w.map, p, a, split, st, pdl()), "fused attention launch");
     return true;
+  }
+
+  // Batch-1 LayerNorm on load: the plan of a bf16 projection of the hidden
+  // rows qualifies (64-token tile, at most eight K blocks per CTA).
+  bool ln_plan(const Proj& w, int M) const {
+    const int d = e->cfg.hidden;
+    if (w.kind != kKindBf16 || M <= 32 || M > 64 || w.K != d || d % 128 || d > 1024 || w.bias) return false;
+    const int kb = w.K / 64;
+    return (kb + ln_split(w.N, kb) - 1) / ln_split(w.N, kb) <= 8;
+  }
+  // Split-K factor of the normalise-on-load projections: the largest of
+  // 8, 6, 4, 3, 2 that keeps the grid within two CTAs per SM (their operand is
+  // built by the CTA's threads, so more CTAs build it in parallel: measured
+  // 935 vs 1004 us per forward against one CTA per SM; a cluster of 7 packed
+  // badly, 1100 us).
+  int ln_split(int N, int kb) const {
+    const int tiles = N / 128;
+    for (int s : {8, 6, 4, 3, 2})
+      if (s <= kb && tiles * s <= 2 * e->sm_count) return s;
+    return 1;
+  }
+
+  // Projection of LN(h) (weight ln_w) with the statistics the previous
+  // residual projection wrote; store (+ rotary) or GEGLU epilogue.
+  void gemm_ln(const Proj& w, const float* ln_w, int M, int epi, __nv_bfloat16* out, int ldo,
+               const float* rope_cos = nullptr, const float* rope_sin = nullptr, int rope_seq = 0) {
+    if (!on(kCatGemm)) return;
+    const int kb = w.K / 64, bn = 64, split = ln_split(w.N, kb);
+    GemmParams p{};
+    p.M = M;
+    p.N = w.N;
+    p.K = w.K;
+    p.kblocks = kb;
+    p.epilogue = epi;
+    p.out = out;
+    p.ldo = ldo;
+    p.status = e->status_dev;
+    if (split > 1 && (size_t)(w.N / 128) * split * bn * 128 <= kPartialFloats) p.partials = e->gpart;
+    if (rope_cos && epi == kEpiStore) {
+      p.rope_cos = rope_cos;
+      p.rope_sin = rope_sin;
+      p.rope_seq = rope_seq;
+      p.rope_cols = 2 * (w.N / 3);
+    }
+    LnParams ln{};
+    ln.h = e->h;
+    ln.ldh = e->cfg.hidden;
+    ln.w = ln_w;
+    ln.stats = e->lnst;
+    ln.ntiles = e->cfg.hidden / 128;
+    ln.eps = e->cfg.norm_eps;
+    count(launch_gemm_ln(w.map, p, ln, split, st, pdl()), "layernorm gemm launch");
   }
 
   // NVFP4 projection: quantise the bf16 operand per row (scale blocks laid
@@ -557,16 +612,24 @@ struct Fwd {
     // Each residual projection (Wo, Wo2) is followed by add_norm
     // (model.py:15-19): mlp_norm after Wo, the next layer's attn_norm (or the
     // final norm) after Wo2.
+    // One short sequence in bf16 (the latency path): attention runs inside the
+    // Wo projection, and attn_norm / mlp_norm inside the QKV / Wi projections,
+    // from row statistics written by the residual projection before them.
+    const bool short_bf16 = !fp8 && !nv4 && b == 1 && c.layers > 0 && ln_plan(E.wqkv[0], T) &&
+                            ln_plan(E.wi[0], T);
     for (int i = 0; i < c.layers; ++i) {
       const std::string pre = "enc." + std::to_string(i) + ".";
       const bool glob = (i % c.global_every) == 0;
       const float* rc = glob ? E.gcos : E.lcos;
       const float* rs = glob ? E.gsin : E.lsin;
       // The rotary embedding runs in the projection's epilogue.
-      const bool rotated =
-          nv4 ? gemm_nv4(E.wqkv[i], E.n, T, kEpiStore, E.qkv, 3 * d, nullptr, 0, rc, rs, s)
-              : gemm(E.wqkv[i], fp8 ? (const void*)E.n8 : (const void*)E.n, E.n8s, T, kEpiStore, E.qkv, 3 * d,
-                     nullptr, 0, rc, rs, s);
+      bool rotated = true;
+      if (short_bf16 && i > 0)
+        gemm_ln(E.wqkv[i], wptr<float>(e, pre + "attn_norm.w"), T, kEpiStore, E.qkv, 3 * d, rc, rs, s);
+      else
+        rotated = nv4 ? gemm_nv4(E.wqkv[i], E.n, T, kEpiStore, E.qkv, 3 * d, nullptr, 0, rc, rs, s)
+                      : gemm(E.wqkv[i], fp8 ? (const void*)E.n8 : (const void*)E.n, E.n8s, T, kEpiStore, E.qkv,
+                             3 * d, nullptr, 0, rc, rs, s);
       AttnParams a{};
       a.qkv = E.qkv;
       a.ld_qkv = 3 * d;
@@ -579,8 +642,8 @@ struct Fwd {
       a.window = glob ? -1 : c.local_window;
       a.out = E.attn;
       a.ld_out = d;
-      // One short sequence in bf16: attention inside the Wo projection.
       const bool fused = !fp8 && !nv4 && b == 1 && gemm_attn(E.wo[i], a, T);
+      if (short_bf16 && !fused) fail("batch-1 plan: the attention projection did not fuse");
       if (!fused) {
         attention(a, b, c.heads);
         if (fp8 && on(kCatQuant)) {
@@ -597,11 +660,15 @@ struct Fwd {
         else
           gemm(E.wo[i], fp8 ? (const void*)E.a8 : (const void*)E.attn, E.a8s, T, kEpiResidual, nullptr, 0, E.h, d);
       }
-      norm(enc_norm(pre + "mlp_norm.w"));
-      if (nv4)
-        gemm_nv4(E.wi[i], E.n, T, kEpiGeglu, E.g, I, nullptr, 0);
-      else
-        gemm(E.wi[i], fp8 ? (const void*)E.n8 : (const void*)E.n, E.n8s, T, kEpiGeglu, E.g, I, nullptr, 0);
+      if (short_bf16)
+        gemm_ln(E.wi[i], wptr<float>(e, pre + "mlp_norm.w"), T, kEpiGeglu, E.g, I);
+      else {
+        norm(enc_norm(pre + "mlp_norm.w"));
+        if (nv4)
+          gemm_nv4(E.wi[i], E.n, T, kEpiGeglu, E.g, I, nullptr, 0);
+        else
+          gemm(E.wi[i], fp8 ? (const void*)E.n8 : (const void*)E.n, E.n8s, T, kEpiGeglu, E.g, I, nullptr, 0);
+      }
       if (fp8 && on(kCatQuant)) {
         QuantParams q{};
         q.rows = T;
@@ -611,12 +678,18 @@ struct Fwd {
         q.scale = E.g8s;
         count(launch_quant_fp8(q, st, pdl()), "quant launch");
       }
+      const bool last = i + 1 == c.layers;
       if (nv4)
         gemm_nv4(E.wo2[i], E.g, T, kEpiResidual, nullptr, 0, E.h, d);
       else
-        gemm(E.wo2[i], fp8 ? (const void*)E.g8 : (const void*)E.g, E.g8s, T, kEpiResidual, nullptr, 0, E.h, d);
-      // add_norm after Wo2: the next layer's attn_norm, or the final norm
-      norm(i + 1 < c.layers ? enc_norm("enc." + std::to_string(i + 1) + ".attn_norm.w") : final_norm);
+        gemm(E.wo2[i], fp8 ? (const void*)E.g8 : (const void*)E.g, E.g8s, T, kEpiResidual, nullptr, 0, E.h, d,
+             nullptr, nullptr, 0, short_bf16 && !last);
+      // add_norm after Wo2: the next layer's attn_norm (applied by its QKV
+      // projection on the batch-1 path), or the final norm
+      if (last)
+        norm(final_norm);
+      else if (!short_bf16)
+        norm(enc_norm("enc." + std::to_string(i + 1) + ".attn_norm.w"));
     }
     // Head layers (model.py:58-70): norm1 of layer j > 0 follows the previous
     // layer's linear2, norm2 follows out_proj.
@@ -857,6 +930,7 @@ int laya_b200_create(int device, const laya_b200_config* cfg, laya_b200_engine**
         {(void**)&e->lsin, (size_t)c.max_len * 64 * 4},
         {(void**)&e->a1, (size_t)c.max_batch * c.act_hidden * 4},
         {(void**)&e->gpart, kPartialFloats * 4},
+        {(void**)&e->lnst, T * (size_t)(d / 128) * 8},
         {(void**)&e->x4, T * (size_t)(d > I ? d : I) / 2},
         {(void**)&e->x4sf, ((T + 15) / 16) * (size_t)(4 * ((std::max(d, I) + 255) / 256)) * 512},
         {(void**)&e->x4o, T * 4},

@@ -44,7 +44,9 @@ struct GemmCfg {
   static constexpr int K_ELEMS = KIND == kKindBf16 ? 64 : 128;
 };
 
-template <int BN, int KIND, int STAGES>
+// LNST: the residual epilogue also writes LayerNorm row statistics
+// (p.ln_stats) for a following projection that normalises on load.
+template <int BN, int KIND, int STAGES, bool LNST = false>
 __global__ void __launch_bounds__(BN >= 128 ? 256 : 128, BN == 128 ? 2 : 1)
     gemm_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ CUtensorMap xmap,
                 const __grid_constant__ CUtensorMap omap, const GemmParams p) {
@@ -156,7 +158,7 @@ __global__ void __launch_bounds__(BN >= 128 ? 256 : 128, BN == 128 ? 2 : 1)
   if (split == 1 && p.tma_epilogue && BN >= 128)
     tile_epilogue_wide<BN, KIND, 256>(p, &omap, tmem, smem, tile_n, tile_m);
   else
-    tile_epilogue<BN, KIND>(p, tmem, reinterpret_cast<float*>(smem), tile_n, tile_m, split, rank);
+    tile_epilogue<BN, KIND, LNST>(p, tmem, reinterpret_cast<float*>(smem), tile_n, tile_m, split, rank);
 
   // ---- teardown: drain copies still in flight after a failure, free TMEM
   if (tid == 0 && *failed) {
@@ -172,12 +174,12 @@ __global__ void __launch_bounds__(BN >= 128 ? 256 : 128, BN == 128 ? 2 : 1)
 
 namespace {
 
-template <int BN, int KIND, int STAGES>
+template <int BN, int KIND, int STAGES, bool LNST = false>
 cudaError_t launch_one(const CUtensorMap& wmap, const CUtensorMap& xmap, const CUtensorMap& omap, const GemmParams& p,
                        int tiles_n,
                        int tiles_m, int split, cudaStream_t stream, bool pdl) {
   using C = GemmCfg<BN, KIND, STAGES>;
-  auto kern = gemm_kernel<BN, KIND, STAGES>;
+  auto kern = gemm_kernel<BN, KIND, STAGES, LNST>;
   // Function attributes are per device: set them once for each device used.
   static std::mutex mu;
   static uint64_t ready = 0;
@@ -277,6 +279,11 @@ cudaError_t launch_gemm(int kind, const CUtensorMap& wmap, const CUtensorMap& xm
   const int tiles_n = p.N / 128;
   const int tiles_m = (p.M + bn - 1) / bn;
   if (p.N % 128 || split < 1 || split > 16 || split > p.kblocks) return cudaErrorInvalidValue;
+  if (p.ln_stats) {  // batch-1 residual projection feeding a normalise-on-load projection
+    if (kind != kKindBf16 || bn != 64 || p.epilogue != kEpiResidual || p.bias || (split == 1 && p.tma_epilogue))
+      return cudaErrorInvalidValue;
+    return launch_one<64, kKindBf16, 4, true>(wmap, xmap, omap, p, tiles_n, tiles_m, split, stream, pdl);
+  }
   if (kind == kKindBf16) return dispatch_bn<kKindBf16>(bn, wmap, xmap, omap, p, tiles_n, tiles_m, split, stream, pdl);
   if (kind == kKindFp8) return dispatch_bn<kKindFp8>(bn, wmap, xmap, omap, p, tiles_n, tiles_m, split, stream, pdl);
   return cudaErrorInvalidValue;

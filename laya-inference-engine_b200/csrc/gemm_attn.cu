@@ -13,8 +13,10 @@
 // kernel's tile arithmetic and write the bf16 output straight into the MMA's
 // B operand stage, in the 128-byte-swizzled K-major layout a TMA load would
 // have produced.  The MMA, the split-K reduction and the residual epilogue are
-// the projection GEMM's.  Every CTA recomputes its heads for its own weight
-// tile: at 64 tokens that is cheaper than a separate launch.
+// the projection GEMM's; the epilogue also writes the LayerNorm statistics of
+// the updated residual rows for the MLP projection, which normalises on load.
+// Every CTA recomputes its heads for its own weight tile: at 64 tokens that is
+// cheaper than a separate launch.
 #include "common.cuh"
 #include "params.h"
 #include "launch.h"
@@ -154,7 +156,7 @@ __global__ void __launch_bounds__(kFaThreads, 1)
     atomicExch(failed, 1u);
   }
   tc_fence_after();
-  tile_epilogue<kFaBN, kKindBf16>(p, tmem, reinterpret_cast<float*>(smem), tile_n, 0, split, rank);
+  tile_epilogue<kFaBN, kKindBf16, true>(p, tmem, reinterpret_cast<float*>(smem), tile_n, 0, split, rank);
 
   // teardown: drain weight copies still in flight after a failure, free TMEM
   if (tid == 0 && *failed)
@@ -167,7 +169,8 @@ __global__ void __launch_bounds__(kFaThreads, 1)
 cudaError_t launch_gemm_attn(const CUtensorMap& wmap, const GemmParams& p, const AttnParams& a, int split,
                              cudaStream_t stream, bool pdl) {
   if (p.N % 128 || p.M <= 32 || p.M > kFaBN || a.s != p.M || split < 1 || split > 16 || split > p.kblocks ||
-      p.kblocks * 64 != p.K || p.K != a.d || p.epilogue != kEpiResidual || a.q_pos || a.nq != a.s || a.cos)
+      p.kblocks * 64 != p.K || p.K != a.d || p.epilogue != kEpiResidual || a.q_pos || a.nq != a.s || a.cos ||
+      !p.ln_stats || p.bias)
     return cudaErrorInvalidValue;
   if ((p.kblocks + split - 1) / split > kFaStages) return cudaErrorInvalidValue;
   static std::mutex mu;

@@ -143,7 +143,9 @@ DEVI void epilogue_rope(const GemmParams& p, int m, int n_lo, float4 lo, float4 
 // Called by all 128 threads after the MMA-done barrier completed.
 // `part` is this CTA's shared scratch of at least BN*128 floats (the
 // pipeline region, free once every MMA has completed).
-template <int BN, int KIND>
+// LNST: residual epilogue that also writes the LayerNorm statistics of the
+// updated rows (p.ln_stats; bf16 projections without bias).
+template <int BN, int KIND, bool LNST = false>
 DEVI void tile_epilogue(const GemmParams& p, uint32_t tmem, float* part, int tile_n, int tile_m, int split,
                         int rank) {
   const int tid = threadIdx.x, warp = tid >> 5;
@@ -222,6 +224,32 @@ DEVI void tile_epilogue(const GemmParams& p, uint32_t tmem, float* part, int til
             hi.x += vb[u].x; hi.y += vb[u].y; hi.z += vb[u].z; hi.w += vb[u].w;
           }
       }
+    }
+    if (LNST) {
+      // residual update, then the tile statistics of token m: its 16 items
+      // are 16 consecutive threads (a 16-lane half warp)
+      float4* rl = reinterpret_cast<float4*>(p.resid + (size_t)m * p.ldr + tile_n * 128 + q4);
+      float4* rh = rl + 16;
+      float4 a = *rl, b = *rh;
+      a.x += bf16_round(lo.x); a.y += bf16_round(lo.y); a.z += bf16_round(lo.z); a.w += bf16_round(lo.w);
+      b.x += bf16_round(hi.x); b.y += bf16_round(hi.y); b.z += bf16_round(hi.z); b.w += bf16_round(hi.w);
+      *rl = a;
+      *rh = b;
+      const unsigned half = 0xFFFFu << (tid & 16);
+      float sum = (a.x + a.y + a.z + a.w) + (b.x + b.y + b.z + b.w);
+#pragma unroll
+      for (int o = 8; o > 0; o >>= 1) sum += __shfl_xor_sync(half, sum, o);
+      const float mean = sum * (1.0f / 128.0f);
+      float m2 = 0.f;
+      {
+        const float v[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+#pragma unroll
+        for (int e = 0; e < 8; ++e) m2 += (v[e] - mean) * (v[e] - mean);
+      }
+#pragma unroll
+      for (int o = 8; o > 0; o >>= 1) m2 += __shfl_xor_sync(half, m2, o);
+      if ((tid & 15) == 0) p.ln_stats[(size_t)m * gridDim.x + tile_n] = make_float2(mean, m2);
+      continue;
     }
     if (rope)
       epilogue_rope<KIND>(p, m, tile_n * 128 + q4, lo, hi);

@@ -19,6 +19,12 @@ cudaError_t launch_gemm(int kind, const CUtensorMap& wmap, const CUtensorMap& xm
 // heads computed in shared memory as the B operand (gemm_attn.cu).
 cudaError_t launch_gemm_attn(const CUtensorMap& wmap, const GemmParams& p, const AttnParams& a, int split,
                              cudaStream_t stream, bool pdl);
+// Projection (store / GEGLU epilogue) of LN(h) for one sequence of
+// 32 < s <= 64 tokens (bf16): the LayerNorm is applied while the operand is
+// built, from the row statistics of the previous residual projection
+// (gemm_ln.cu).
+cudaError_t launch_gemm_ln(const CUtensorMap& wmap, const GemmParams& p, const LnParams& ln, int split,
+                           cudaStream_t stream, bool pdl);
 cudaError_t launch_gemm_nvfp4(const CUtensorMap& wmap, const CUtensorMap& xmap, const CUtensorMap& omap,
                               const uint8_t* wsf,
                               const uint8_t* xsf, int sf_kbs, const GemmParams& p, int bn, int split,

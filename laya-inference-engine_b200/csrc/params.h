@@ -71,6 +71,23 @@ struct GemmParams {
   int rope_seq;
   int rope_cols;
   float* partials;           // global split-K partials [tiles][split][BN][128] floats, or null
+  // Residual projections feeding a LayerNorm that the next projection applies
+  // on load: per (token, 128-column tile) statistics of the updated residual
+  // row, (mean, sum of squared deviations) over the tile, at
+  // [token * (N / 128) + tile].
+  float2* ln_stats;
+};
+
+// LayerNorm applied by a projection to its fp32 input rows while building the
+// bf16 operand (batch-1 path): LN(h) * w with the row statistics merged from
+// the per-tile partials the previous residual projection wrote.
+struct LnParams {
+  const float* h;           // fp32 [M][ldh] residual rows
+  int ldh;
+  const float* w;           // LayerNorm weight [K]
+  const float2* stats;      // [M][ntiles] (mean, M2) over 128-column tiles
+  int ntiles;               // K / 128
+  float eps;
 };
 
 

@@ -189,9 +189,10 @@ def test_fp8_activation_quantiser_is_bit_exact(intermediate):
 
 @pytest.mark.parametrize("s,length", [(64, 64), (64, 37), (40, 40)])
 def test_fused_attention_projection_matches_oracle(s, length):
-    """One short sequence in bf16 runs attention inside the Wo projection
-    (one launch per layer instead of two): whole forward against the oracle on
-    a network with global and radius-64 local layers, full and key-padded."""
+    """One short sequence in bf16 runs attention inside the Wo projection and
+    attn_norm / mlp_norm inside the QKV / Wi projections: whole forward
+    against the oracle on a network with global and radius-64 local layers,
+    full and key-padded."""
     from laya_b200.engine import NativeForward
     cfg = MICRO_LOCAL
     w = seeded_weights(cfg, seed=9)
@@ -204,10 +205,11 @@ def test_fused_attention_projection_matches_oracle(s, length):
         ol, oa = O.Oracle(w, cfg).forward(**inp)
         mm = inp["marker_mask"]
         assert np.abs(logits[mm] - ol[mm]).max() < 2e-2 and np.abs(act - oa).max() < 2e-2
-        # the fused path is the one that ran: one launch fewer per layer than
-        # the same sequence length at batch 2
+        # the fused path is the one that ran: against the same sequence length
+        # at batch 2, no attention launch per layer and no mlp_norm / attn_norm
+        # launches inside the encoder
         two = nf.capture(2, s, 4, False)
-        assert nf.kernel_count(slot) == nf.kernel_count(two) - cfg.layers
+        assert nf.kernel_count(slot) == nf.kernel_count(two) - cfg.layers - (2 * cfg.layers - 1)
     finally:
         nf.close()
 
