@@ -72,20 +72,34 @@ def peaks():
 
 
 def gemm_bytes(cfg, b, s, k, precision):
-    """Algorithmic bytes of one forward's projection GEMMs: each weight read
+    """Algorithmic bytes of one forward's projection kernels: each weight read
     once (plus fp8 row scales), each activation operand read once, each output
-    written once (a residual epilogue reads and writes fp32)."""
+    written once (a residual epilogue reads and writes fp32).  On the batch-1
+    bf16 path (32 < s <= 64) the Wo kernel reads q, k, v (attention fused) and
+    writes LayerNorm tile statistics, and the QKV (layers > 0) / Wi kernels read
+    the fp32 rows, their statistics and the norm weight (LayerNorm on load)."""
     T, R, BK = b * s, b * (1 + k), b * k
     d, I, F = cfg.hidden, cfg.intermediate, cfg.head_ff
     wb = 1 if precision == "fp8" else 2
+    short = precision == "bf16" and b == 1 and 32 < s <= 64
+    stats = T * (d // 128) * 8
     total, launches = 0, 0
 
-    def g(M, N, K, wbytes, xbytes, obytes):
+    def g(M, N, K, wbytes, xbytes, obytes, extra=0):
         nonlocal total, launches
-        total += N * K * wbytes + M * K * xbytes + M * N * obytes + (N * 4 if wbytes == 1 else 0)
+        total += N * K * wbytes + M * K * xbytes + M * N * obytes + (N * 4 if wbytes == 1 else 0) + extra
         launches += 1
 
-    for _ in range(cfg.layers):
+    for i in range(cfg.layers):
+        if short:
+            if i == 0:
+                g(T, 3 * d, d, 2, 2, 2)
+            else:
+                g(T, 3 * d, d, 2, 4, 2, stats + 4 * d)          # LN(h) on load
+            g(T, d, d, 2, 0, 8, T * 3 * d * 2 + stats)          # q, k, v in; statistics out
+            g(T, 2 * I, d, 2, 4, 1, stats + 4 * d)              # LN(h) on load, GEGLU out
+            g(T, d, I, 2, 2, 8, stats if i + 1 < cfg.layers else 0)
+            continue
         g(T, 3 * d, d, wb, wb, 2)
         g(T, d, d, wb, wb, 8)
         g(T, 2 * I, d, wb, wb, 1)   # GEGLU writes I outputs for 2I rows
@@ -428,7 +442,9 @@ def main():
                        "l2": f"inputs larger than L2: {fwd_bytes / 1e6:.0f} MB of weights streamed per step"},
             "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                     "path": "B200Engine.run_prepared -> laya_b200_run (pinned pack, H2D, graph, D2H)"},
-            "roofline": {"bound": "hbm", "kernel": "gemm_kernel (all projection GEMMs of one forward)",
+            "roofline": {"bound": "hbm",
+                         "kernel": "projection kernels of one forward: gemm_kernel, gemm_attn_kernel (Wo with the "
+                                   "attention fused), gemm_ln_kernel (QKV / Wi with LayerNorm on load)",
                          "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
                          "traffic": traffic, "peak_source": peak_kind,
                          "launches_per_forward": glaunch, "algorithmic_bytes_per_launch": gbytes / glaunch,
