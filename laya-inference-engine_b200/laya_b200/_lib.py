@@ -55,15 +55,15 @@ def load():
                            "(the b200 mode has no CPU fallback)")
     lib = ctypes.CDLL(str(LIB_PATH))
     P, I, F = ctypes.c_void_p, ctypes.c_int, ctypes.POINTER(ctypes.c_float)
-    i64p = ctypes.POINTER(ctypes.c_int64)
-    u8p = ctypes.POINTER(ctypes.c_uint8)
     sig = {
         "laya_b200_create": (I, [I, ctypes.POINTER(Config), ctypes.POINTER(P)]),
         "laya_b200_set_weight": (I, [P, ctypes.c_char_p, P, ctypes.c_size_t]),
         "laya_b200_finalize": (I, [P, I]),
         "laya_b200_capture": (I, [P, I, I, I, I, ctypes.POINTER(I)]),
         "laya_b200_release": (I, [P, I]),
-        "laya_b200_run": (I, [P, I, i64p, i64p, i64p, u8p, i64p, F, F]),
+        # host arrays by address (int64 ids / mask / marker_pos / qtype, uint8
+        # marker_mask, fp32 logits / act)
+        "laya_b200_run": (I, [P, I, P, P, P, P, P, P, P]),
         "laya_b200_replay_device": (I, [P, I, I, I, F]),
         "laya_b200_kernel_count": (I, [P, I, ctypes.POINTER(I)]),
         "laya_b200_read_buffer": (I, [P, ctypes.c_char_p, P, ctypes.c_size_t]),

@@ -9,7 +9,7 @@ import pytest
 from laya_b200.config import TINY
 from laya_b200.engine import B200Engine, request_from_items, _device_index
 from laya_b200.protocol import PreparedRequest
-from laya_b200.workload import pack
+from laya_b200.workload import pack, synthetic_items
 
 
 class FakeNative:
@@ -155,3 +155,44 @@ def test_request_from_items_counts_tokens():
     items = [{"ids": [1, 2, 3], "markers": [1, 2], "qtype": 0}, {"ids": [4], "markers": [0, 0], "qtype": 2}]
     req = request_from_items(items)
     assert req.input_tokens == 4 and len(req.ids) == 2
+
+
+class AddressNative(FakeNative):
+    """A native stand-in that reads run()'s host arrays back from their
+    addresses, as the C ABI does."""
+
+    def __init__(self):
+        super().__init__()
+        self.seen = []
+
+    def run_addresses(self, slot, addresses):
+        import ctypes
+        b, s, k = self.captured[slot][:3]
+        def view(addr, shape, dtype):
+            n = int(np.prod(shape)) * np.dtype(dtype).itemsize
+            return np.frombuffer((ctypes.c_char * n).from_address(addr), dtype=dtype).reshape(shape).copy()
+        ids, mask, mpos, mmask, qtype = (view(addresses[0], (b, s), np.int64), view(addresses[1], (b, s), np.int64),
+                                         view(addresses[2], (b, k), np.int64), view(addresses[3], (b, k), np.uint8),
+                                         view(addresses[4], (b,), np.int64))
+        self.seen.append({"input_ids": ids, "attention_mask": mask, "marker_pos": mpos,
+                          "marker_mask": mmask.astype(bool), "qtype": qtype})
+        logits = np.frombuffer((ctypes.c_char * (b * k * 4)).from_address(addresses[5]), np.float32)
+        logits[:] = float(slot)
+
+
+def test_run_packs_into_kept_host_arrays_like_fill():
+    """run_prepared's in-place packing into per-slot host arrays gives the
+    arrays _fill builds (BlackwellEngine._fill semantics), across calls that
+    reuse the arrays with fewer questions and shorter rows."""
+    engine = make_engine(max_questions=4)
+    engine.native = AddressNative()
+    first = synthetic_items([64, 40, 12], ["choice", "noul", "score"], seed=4, vocab=1000)
+    second = synthetic_items([30, 20], ["noul", "noul"], seed=5, vocab=1000)
+    for items in (first, second, first):
+        prepared = request_from_items(items)
+        engine.run_prepared(prepared)
+        shape = engine._shape(prepared)
+        want = engine._fill(prepared, shape)
+        got = engine.native.seen[-1]
+        for name in want:
+            assert np.array_equal(got[name], want[name]), name
