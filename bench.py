@@ -51,6 +51,8 @@ def parse():
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--precision", default="bf16", choices=["bf16", "fp8"])
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
+    ap.add_argument("--lanes", type=int, default=2,
+                    help="c1: also time this many serving lanes replaying at once (1: skip)")
     ap.add_argument("--workload", default="c1", choices=["c1", "c2", "c3", "c4"],
                     help="c1 (default, the contract line): b=1 s=64 noul; c2: FP8 16x96; c3: NVFP4 1x512; "
                          "c4: FP8 64 questions s~U[32,512] bucketed by 32, sharded over ranks")
@@ -367,7 +369,7 @@ def main():
     from laya_b200.engine import B200Engine, request_from_items
     cfg = LAYA
     eng = B200Engine(config=cfg, device=local, precision=args.precision, max_questions=1, max_options=2,
-                     max_graphs=2)
+                     max_graphs=2, lanes=max(1, args.lanes))
     items, inp = workload(cfg, seed=rank)
     prepared = request_from_items(items)
     logits, act, meta = eng.run_prepared(prepared)  # captures the graph, inputs now resident
@@ -412,6 +414,35 @@ def main():
     h2d = 4 * (2 * b * s + b + 2 * b * k + 2 * b * (1 + k))
     d2h = 4 * (b * k + 2 * b)
 
+    # ---- serving lanes: the same request replayed on every lane at once
+    # (one GPU serving several requests concurrently); supplementary to the
+    # single-lane value, host wall clock around the concurrent device loops
+    lanes_line = None
+    if args.lanes > 1:
+        key = (1, 64, 2, True)
+        lane_slots = []
+        for lane in eng._lanes:
+            eng._run_on(prepared, lane)          # captures the lane's graph
+            lane_slots.append((lane.native, lane.graphs[key]))
+            lane.native.replay_device(lane.graphs[key], args.warmup)
+        lane_ms = [None] * len(lane_slots)
+
+        def replay(i):
+            lane_ms[i] = lane_slots[i][0].replay_device(lane_slots[i][1], args.steps)
+
+        threads = [threading.Thread(target=replay, args=(i,)) for i in range(len(lane_slots))]
+        barrier()
+        t0 = time.perf_counter()
+        for t in threads:
+            t.start()
+        for t in threads:
+            t.join()
+        lanes_s = max_over_ranks(time.perf_counter() - t0)
+        barrier()
+        lanes_line = {"lanes": len(lane_slots), "value": world * len(lane_slots) * args.steps / lanes_s,
+                      "unit": UNIT, "p50_ms": float(np.median(np.concatenate(lane_ms))),
+                      "timing": "host wall clock around concurrent device replay loops, one per lane"}
+
     # ---- roofline of the dominant kernel family (projection GEMMs)
     gms = native.replay_device(slot, max(20, min(args.steps, 500)), kernel_mask=1)
     gemm_ms = float(np.mean(gms))
@@ -452,6 +483,7 @@ def main():
             "forward_roofline": {"bytes_alg": fwd_bytes, "achieved_gbs": fwd_achieved,
                                  "frac": fwd_achieved / peak},
             "cpu_baseline": {k: base[k] for k in ("value", "unit", "cores", "kind", "sample")},
+            **({"serving_lanes": lanes_line} if lanes_line else {}),
             "gpu_launches": kernels * args.steps,
             "kernels_per_forward": kernels,
             "clocks": cs,

@@ -58,6 +58,16 @@ LAYA_B200_API int laya_b200_set_weight(laya_b200_engine* e, const char* name, co
  * scale) and build the weight tensor maps. */
 LAYA_B200_API int laya_b200_finalize(laya_b200_engine* e, int precision);
 
+/* Serving lanes (the multi-stream lanes of the reference's serving
+ * experiments, experiments/latency/serving/README.md:6-14; no counterpart in
+ * its engine API): a new engine handle on the parent's GPU that shares the
+ * parent's finalized weights and has its own stream, activations, I/O staging
+ * and graph slots, so requests on different lanes run concurrently.  Every
+ * call takes a lane like an engine; the shared weights are freed with the last
+ * of the parent and its lanes.  Calls on one lane must be serialised by the
+ * caller, calls on different lanes may overlap. */
+LAYA_B200_API int laya_b200_create_lane(laya_b200_engine* parent, laya_b200_engine** lane);
+
 /* Capture the forward for one padded shape into CUDA graphs (the analogue
  * of BlackwellEngine._slot, engine.py:161-187).  `unmasked` mirrors the
  * graph key's flag (engine.py:132-138); results do not depend on it. */

@@ -173,6 +173,14 @@ struct Slot {
   bool live = false;
 };
 
+// Weight memory shared by an engine and its lanes; freed with the last one.
+struct WeightShare {
+  std::mutex mu;
+  int refs = 1;
+  uint8_t* warena = nullptr;
+  uint8_t* qarena = nullptr;
+};
+
 }  // namespace
 
 struct laya_b200_engine {
@@ -190,6 +198,7 @@ struct laya_b200_engine {
   size_t warena_bytes = 0;
   uint8_t* qarena = nullptr;  // packed low-precision encoder weights
   size_t qarena_bytes = 0;
+  WeightShare* weights = nullptr;  // owner of warena / qarena (shared with lanes)
 
   // activations
   uint8_t* aarena = nullptr;
@@ -865,6 +874,72 @@ int guard(laya_b200_engine* e, const std::function<void()>& fn) {
 
 }  // namespace
 
+// Stream, activation arena, RoPE tables, I/O staging and status word of one
+// engine or lane (everything but the weights).
+void alloc_runtime(laya_b200_engine* e) {
+  ck(cudaStreamCreateWithFlags(&e->stream, cudaStreamNonBlocking), "stream");
+  ck(cudaEventCreate(&e->ev0), "event");
+  ck(cudaEventCreate(&e->ev1), "event");
+  // activations
+  const laya_b200_config& c = e->cfg;
+  const int d = c.hidden, I = c.intermediate, F = c.head_ff;
+  const size_t T = (size_t)c.max_batch * c.max_len;
+  const size_t R = (size_t)c.max_batch * (1 + c.max_options);
+  const size_t BK = (size_t)c.max_batch * c.max_options;
+  e->max_tokens = (int)T;
+  e->x4_col_blocks = 4 * ((std::max(d, I) + 255) / 256);
+  const size_t gw = (size_t)(I > F ? I : F);
+  std::vector<std::pair<void**, size_t>> bufs = {
+      {(void**)&e->h, T * d * 4},         {(void**)&e->n, T * d * 2},
+      {(void**)&e->qkv, T * 3 * d * 2},   {(void**)&e->attn, T * d * 2},
+      {(void**)&e->g, T * gw * 2},        {(void**)&e->n8, T * d},
+      {(void**)&e->a8, T * d},            {(void**)&e->g8, T * I},
+      {(void**)&e->n8s, T * 4},           {(void**)&e->a8s, T * 4},
+      {(void**)&e->g8s, T * 4},           {(void**)&e->hsel, R * d * 4},
+      {(void**)&e->asel, R * d * 2},      {(void**)&e->nsel, R * d * 2},
+      {(void**)&e->fsel, R * F * 2},      {(void**)&e->msc, BK * d * 2},
+      {(void**)&e->zsc, BK * d * 2},      {(void**)&e->gcos, (size_t)c.max_len * 64 * 4},
+      {(void**)&e->gsin, (size_t)c.max_len * 64 * 4}, {(void**)&e->lcos, (size_t)c.max_len * 64 * 4},
+      {(void**)&e->lsin, (size_t)c.max_len * 64 * 4},
+      {(void**)&e->a1, (size_t)c.max_batch * c.act_hidden * 4},
+      {(void**)&e->gpart, kPartialFloats * 4},
+      {(void**)&e->lnst, T * (size_t)(d / 128) * 8},
+      {(void**)&e->x4, T * (size_t)(d > I ? d : I) / 2},
+      {(void**)&e->x4sf, ((T + 15) / 16) * (size_t)(4 * ((std::max(d, I) + 255) / 256)) * 512},
+      {(void**)&e->x4o, T * 4},
+      {(void**)&e->arrivals, (size_t)c.max_batch * 4},
+  };
+  size_t aoff = 0;
+  for (auto& b : bufs) aoff = align_up(aoff + b.second, 1024);
+  e->aarena_bytes = aoff;
+  ck(cudaMalloc(&e->aarena, aoff), "activation arena");
+  ck(cudaMemset(e->aarena, 0, aoff), "activation memset");
+  aoff = 0;
+  for (auto& b : bufs) {
+    *b.first = e->aarena + aoff;
+    aoff = align_up(aoff + b.second, 1024);
+  }
+  std::vector<float> cs, sn;
+  rope_tables(c.rope_theta_global, c.max_len, cs, sn);
+  ck(cudaMemcpy(e->gcos, cs.data(), cs.size() * 4, cudaMemcpyHostToDevice), "rope upload");
+  ck(cudaMemcpy(e->gsin, sn.data(), sn.size() * 4, cudaMemcpyHostToDevice), "rope upload");
+  rope_tables(c.rope_theta_local, c.max_len, cs, sn);
+  ck(cudaMemcpy(e->lcos, cs.data(), cs.size() * 4, cudaMemcpyHostToDevice), "rope upload");
+  ck(cudaMemcpy(e->lsin, sn.data(), sn.size() * 4, cudaMemcpyHostToDevice), "rope upload");
+  // I/O staging capacity: the layout of the largest shape
+  const IoLayout cap = io_layout(Shape{c.max_batch, c.max_len, c.max_options, 0});
+  e->in_words = cap.words;
+  e->out_words = cap.out_words;
+  ck(cudaMalloc(&e->d_in, e->in_words * 4), "input buffer");
+  ck(cudaMemset(e->d_in, 0, e->in_words * 4), "input memset");
+  ck(cudaMalloc(&e->d_out, e->out_words * 4), "output buffer");
+  ck(cudaHostAlloc(&e->h_in, e->in_words * 4, cudaHostAllocDefault), "pinned input");
+  ck(cudaHostAlloc(&e->h_out, e->out_words * 4, cudaHostAllocDefault), "pinned output");
+  ck(cudaHostAlloc(&e->status_host, 64, cudaHostAllocMapped), "status word");
+  memset(e->status_host, 0, 64);
+  ck(cudaHostGetDevicePointer((void**)&e->status_dev, e->status_host, 0), "status pointer");
+}
+
 extern "C" {
 
 int laya_b200_create(int device, const laya_b200_config* cfg, laya_b200_engine** out) {
@@ -890,9 +965,6 @@ int laya_b200_create(int device, const laya_b200_config* cfg, laya_b200_engine**
       const char* v = getenv("LAYA_B200_SYNC_CHECK");
       e->sync_check = v && v[0] == '1';
     }
-    ck(cudaStreamCreateWithFlags(&e->stream, cudaStreamNonBlocking), "stream");
-    ck(cudaEventCreate(&e->ev0), "event");
-    ck(cudaEventCreate(&e->ev1), "event");
     // weights
     size_t off = 0;
     for (auto& t : param_table(*cfg)) {
@@ -906,66 +978,59 @@ int laya_b200_create(int device, const laya_b200_config* cfg, laya_b200_engine**
       e->params[std::get<0>(t)] = pi;
     }
     e->warena_bytes = off;
-    ck(cudaMalloc(&e->warena, off), "weight arena");
-    // activations
-    const laya_b200_config& c = *cfg;
-    const int d = c.hidden, I = c.intermediate, F = c.head_ff;
-    const size_t T = (size_t)c.max_batch * c.max_len;
-    const size_t R = (size_t)c.max_batch * (1 + c.max_options);
-    const size_t BK = (size_t)c.max_batch * c.max_options;
-    e->max_tokens = (int)T;
-    e->x4_col_blocks = 4 * ((std::max(d, I) + 255) / 256);
-    const size_t gw = (size_t)(I > F ? I : F);
-    std::vector<std::pair<void**, size_t>> bufs = {
-        {(void**)&e->h, T * d * 4},         {(void**)&e->n, T * d * 2},
-        {(void**)&e->qkv, T * 3 * d * 2},   {(void**)&e->attn, T * d * 2},
-        {(void**)&e->g, T * gw * 2},        {(void**)&e->n8, T * d},
-        {(void**)&e->a8, T * d},            {(void**)&e->g8, T * I},
-        {(void**)&e->n8s, T * 4},           {(void**)&e->a8s, T * 4},
-        {(void**)&e->g8s, T * 4},           {(void**)&e->hsel, R * d * 4},
-        {(void**)&e->asel, R * d * 2},      {(void**)&e->nsel, R * d * 2},
-        {(void**)&e->fsel, R * F * 2},      {(void**)&e->msc, BK * d * 2},
-        {(void**)&e->zsc, BK * d * 2},      {(void**)&e->gcos, (size_t)c.max_len * 64 * 4},
-        {(void**)&e->gsin, (size_t)c.max_len * 64 * 4}, {(void**)&e->lcos, (size_t)c.max_len * 64 * 4},
-        {(void**)&e->lsin, (size_t)c.max_len * 64 * 4},
-        {(void**)&e->a1, (size_t)c.max_batch * c.act_hidden * 4},
-        {(void**)&e->gpart, kPartialFloats * 4},
-        {(void**)&e->lnst, T * (size_t)(d / 128) * 8},
-        {(void**)&e->x4, T * (size_t)(d > I ? d : I) / 2},
-        {(void**)&e->x4sf, ((T + 15) / 16) * (size_t)(4 * ((std::max(d, I) + 255) / 256)) * 512},
-        {(void**)&e->x4o, T * 4},
-        {(void**)&e->arrivals, (size_t)c.max_batch * 4},
-    };
-    size_t aoff = 0;
-    for (auto& b : bufs) aoff = align_up(aoff + b.second, 1024);
-    e->aarena_bytes = aoff;
-    ck(cudaMalloc(&e->aarena, aoff), "activation arena");
-    ck(cudaMemset(e->aarena, 0, aoff), "activation memset");
-    aoff = 0;
-    for (auto& b : bufs) {
-      *b.first = e->aarena + aoff;
-      aoff = align_up(aoff + b.second, 1024);
-    }
-    std::vector<float> cs, sn;
-    rope_tables(c.rope_theta_global, c.max_len, cs, sn);
-    ck(cudaMemcpy(e->gcos, cs.data(), cs.size() * 4, cudaMemcpyHostToDevice), "rope upload");
-    ck(cudaMemcpy(e->gsin, sn.data(), sn.size() * 4, cudaMemcpyHostToDevice), "rope upload");
-    rope_tables(c.rope_theta_local, c.max_len, cs, sn);
-    ck(cudaMemcpy(e->lcos, cs.data(), cs.size() * 4, cudaMemcpyHostToDevice), "rope upload");
-    ck(cudaMemcpy(e->lsin, sn.data(), sn.size() * 4, cudaMemcpyHostToDevice), "rope upload");
-    // I/O staging capacity: the layout of the largest shape
-    const IoLayout cap = io_layout(Shape{c.max_batch, c.max_len, c.max_options, 0});
-    e->in_words = cap.words;
-    e->out_words = cap.out_words;
-    ck(cudaMalloc(&e->d_in, e->in_words * 4), "input buffer");
-    ck(cudaMemset(e->d_in, 0, e->in_words * 4), "input memset");
-    ck(cudaMalloc(&e->d_out, e->out_words * 4), "output buffer");
-    ck(cudaHostAlloc(&e->h_in, e->in_words * 4, cudaHostAllocDefault), "pinned input");
-    ck(cudaHostAlloc(&e->h_out, e->out_words * 4, cudaHostAllocDefault), "pinned output");
-    ck(cudaHostAlloc(&e->status_host, 64, cudaHostAllocMapped), "status word");
-    memset(e->status_host, 0, 64);
-    ck(cudaHostGetDevicePointer((void**)&e->status_dev, e->status_host, 0), "status pointer");
+    e->weights = new WeightShare();
+    ck(cudaMalloc(&e->weights->warena, off), "weight arena");
+    e->warena = e->weights->warena;
+    alloc_runtime(e.get());
     if (!get_encode_fn()) fail("cuTensorMapEncodeTiled is unavailable");
+  } catch (const Error& err) {
+    g_create_error = err.msg;
+    laya_b200_destroy(e.release());
+    return 1;
+  }
+  *out = e.release();
+  return 0;
+}
+
+int laya_b200_create_lane(laya_b200_engine* parent, laya_b200_engine** out) {
+  if (!out || !parent) {
+    g_create_error = "null argument";
+    return 1;
+  }
+  *out = nullptr;
+  if (!parent->finalized) {
+    g_create_error = "finalize the weights before creating a lane";
+    return 1;
+  }
+  std::unique_ptr<laya_b200_engine> e(new laya_b200_engine());
+  try {
+    ck(cudaSetDevice(parent->device), "cudaSetDevice");
+    e->device = parent->device;
+    e->cfg = parent->cfg;
+    e->sm_count = parent->sm_count;
+    e->sync_check = parent->sync_check;
+    e->precision = parent->precision;
+    e->params = parent->params;
+    {
+      std::lock_guard<std::mutex> lock(parent->weights->mu);
+      parent->weights->refs++;
+    }
+    e->weights = parent->weights;
+    e->warena = parent->warena;
+    e->warena_bytes = parent->warena_bytes;
+    e->qarena = parent->qarena;
+    e->qarena_bytes = parent->qarena_bytes;
+    e->wqkv = parent->wqkv;
+    e->wo = parent->wo;
+    e->wi = parent->wi;
+    e->wo2 = parent->wo2;
+    e->in_proj = parent->in_proj;
+    e->out_proj = parent->out_proj;
+    e->lin1 = parent->lin1;
+    e->lin2 = parent->lin2;
+    e->sc_fc1 = parent->sc_fc1;
+    e->finalized = true;
+    alloc_runtime(e.get());
   } catch (const Error& err) {
     g_create_error = err.msg;
     laya_b200_destroy(e.release());
@@ -1033,6 +1098,7 @@ int laya_b200_finalize(laya_b200_engine* e, int precision) {
         }
       e->qarena_bytes = off;
       ck(cudaMalloc(&e->qarena, off), "packed weight arena");
+      e->weights->qarena = e->qarena;
       for (auto& q : qoff) {
         const ParamInfo& pi = e->params.at(q.first);
         uint8_t* wq = e->qarena + q.second;
@@ -1068,6 +1134,7 @@ int laya_b200_finalize(laya_b200_engine* e, int precision) {
       off = align_up(off + 4, 256);
       e->qarena_bytes = off;
       ck(cudaMalloc(&e->qarena, off), "packed weight arena");
+      e->weights->qarena = e->qarena;
       ck(cudaMemset(e->qarena, 0, off), "packed weight arena");  // zero scale padding
       for (auto& w : nv4) {
         const ParamInfo& pi = e->params.at(w.name);
@@ -1288,8 +1355,18 @@ int laya_b200_destroy(laya_b200_engine* e) {
   cudaSetDevice(e->device);
   if (e->stream) cudaStreamSynchronize(e->stream);
   for (auto& s : e->slots) free_slot(s);
-  cudaFree(e->warena);
-  cudaFree(e->qarena);
+  if (e->weights) {
+    int left;
+    {
+      std::lock_guard<std::mutex> lock(e->weights->mu);
+      left = --e->weights->refs;
+    }
+    if (left == 0) {
+      cudaFree(e->weights->warena);
+      cudaFree(e->weights->qarena);
+      delete e->weights;
+    }
+  }
   cudaFree(e->aarena);
   cudaFree(e->d_in);
   cudaFree(e->d_out);

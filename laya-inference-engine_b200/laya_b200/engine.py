@@ -17,6 +17,7 @@ The forward itself runs in liblaya_b200.so; there is no CPU path.
 """
 from collections import OrderedDict
 import ctypes
+import queue
 import threading
 import time
 
@@ -120,10 +121,33 @@ class NativeForward:
         _lib.check(self.lib, self.handle, st, f"read_buffer({name})")
         return out
 
+    def lane(self):
+        """A serving lane: another handle on the same GPU sharing these
+        weights, with its own stream, activations and graphs."""
+        handle = ctypes.c_void_p()
+        if self.lib.laya_b200_create_lane(self.handle, ctypes.byref(handle)) != 0:
+            msg = self.lib.laya_b200_last_error(None)
+            raise RuntimeError(f"laya_b200_create_lane: {msg.decode() if msg else 'unknown error'}")
+        other = NativeForward.__new__(NativeForward)
+        other.lib, other.cfg, other.precision, other.device = self.lib, self.cfg, self.precision, self.device
+        other.max_batch, other.max_options = self.max_batch, self.max_options
+        other.handle = handle
+        return other
+
     def close(self):
         if getattr(self, "handle", None):
             self.lib.laya_b200_destroy(self.handle)
             self.handle = None
+
+
+class _Lane:
+    """Per-lane state of a B200Engine beyond lane 0 (which is the engine's own
+    native / graphs / _io)."""
+
+    def __init__(self, native):
+        self.native = native
+        self.graphs = OrderedDict()
+        self._io = {}
 
 
 class B200Engine:
@@ -132,9 +156,11 @@ class B200Engine:
     def __init__(self, model=None, *, weights=None, config: LayaConfig = LAYA, seed=0, device="cuda:0",
                  max_graphs=8, max_questions=64, sequence_buckets=(64, 128, 256, 384, 512, 768, 1024),
                  precision="bf16", max_options=256, tokenizer=None, agent_cfg=None, temperature=None,
-                 temperature_by_options=None):
+                 temperature_by_options=None, lanes=1):
         if max_graphs < 1 or max_questions < 1:
             raise ValueError("max_graphs and max_questions must be positive")
+        if lanes < 1:
+            raise ValueError("lanes must be positive")
         if precision not in _lib.PRECISIONS:
             raise ValueError("precision must be bf16, fp8 or nvfp4")
         self.device = _device_index(device)
@@ -157,6 +183,21 @@ class B200Engine:
         self.native = NativeForward(self.device, config, weights, precision, max_batch=max_questions,
                                     max_options=max_options)
         self.max_options = max_options
+        # Serving lanes: requests from concurrent callers run on idle lanes
+        # (lane 0 is this object's own native / graphs); one lane serialises
+        # every call like the reference's engine lock (engine.py:84,192).
+        self._idle = queue.Queue()
+        self._lanes = [self]
+        try:
+            for _ in range(lanes - 1):
+                self._lanes.append(_Lane(self.native.lane()))
+        except Exception:
+            for lane in self._lanes[1:]:
+                lane.native.close()
+            self.native.close()
+            raise
+        for lane in self._lanes:
+            self._idle.put(lane)
 
     # -- request preparation (needs the Laya SDK tokenizer, as the reference)
     def prepare(self, state, questions):
@@ -187,14 +228,15 @@ class B200Engine:
         batch, length, options = shape
         return pack(prepared.items, batch, length, options, self.pad_token_id)
 
-    def _run_slot(self, slot, key, prepared):
+    def _run_slot(self, slot, key, prepared, lane=None):
         """Pack into the slot's own host arrays (kept per graph key, addresses
         computed once) and run; same values as _fill + NativeForward.run."""
-        if not hasattr(self.native, "run_addresses"):
-            return self.native.run(slot, self._fill(prepared, key[:3]))
-        io = getattr(self, "_io", None)
+        lane = lane or self
+        if not hasattr(lane.native, "run_addresses"):
+            return lane.native.run(slot, self._fill(prepared, key[:3]))
+        io = getattr(lane, "_io", None)
         if io is None:
-            io = self._io = {}
+            io = lane._io = {}
         bufs = io.get(key)
         if bufs is None:
             batch, length, options = key[:3]
@@ -223,7 +265,7 @@ class B200Engine:
             mpos[i, :k] = item["markers"]
             mmask[i, :k] = 1
             qtype[i] = item["qtype"]
-        self.native.run_addresses(slot, addresses)
+        lane.native.run_addresses(slot, addresses)
         return arrays["logits"], arrays["act"]
 
     def _check_items(self, prepared, shape):
@@ -234,36 +276,49 @@ class B200Engine:
             if len(item["markers"]) > options or len(item["markers"]) > self.max_options:
                 raise ValueError(f"question has {len(item['markers'])} options; maximum is {self.max_options}")
 
-    def _slot(self, prepared, key=None):
+    def _slot(self, prepared, key=None, lane=None):
+        lane = lane or self
         key = key or self._graph_key(prepared)
-        if key in self.graphs:
-            self.graphs.move_to_end(key)
-            return self.graphs[key], False, 0.0
-        if len(self.graphs) >= self.max_graphs:
-            old_key, old = self.graphs.popitem(last=False)
-            self.native.release(old)
-            getattr(self, "_io", {}).pop(old_key, None)
+        if key in lane.graphs:
+            lane.graphs.move_to_end(key)
+            return lane.graphs[key], False, 0.0
+        if len(lane.graphs) >= self.max_graphs:
+            old_key, old = lane.graphs.popitem(last=False)
+            lane.native.release(old)
+            getattr(lane, "_io", {}).pop(old_key, None)
         start = time.perf_counter()
-        slot = self.native.capture(*key)
-        self.graphs[key] = slot
+        slot = lane.native.capture(*key)
+        lane.graphs[key] = slot
         return slot, True, (time.perf_counter() - start) * 1000
 
     def run_prepared(self, prepared):
         """Returns owned CPU arrays (logits [n, k_padded], act [n, 2], metrics)."""
-        with self.lock:
+        idle = getattr(self, "_idle", None)
+        if idle is None:  # engines assembled without lanes
+            with self.lock:
+                if self.closed:
+                    raise RuntimeError("Engine is closed")
+                return self._run_on(prepared, self)
+        lane = idle.get()
+        try:
             if self.closed:
                 raise RuntimeError("Engine is closed")
-            if not prepared.items:
-                return np.empty((0, 0)), np.empty((0, 2)), {"graph_miss": False}
-            key = self._graph_key(prepared)
-            shape = key[:3]
-            self._check_items(prepared, shape)
-            slot, miss, build_ms = self._slot(prepared, key)
-            logits, act = self._run_slot(slot, key, prepared)
-            count = len(prepared.items)
-            return logits[:count].copy(), act[:count].copy(), {
-                "graph_miss": miss, "graph_build_ms": build_ms if miss else 0.0, "shape": list(shape),
-                "backend": self.backend, "precision": self.precision, "device": f"cuda:{self.device}"}
+            return self._run_on(prepared, lane)
+        finally:
+            idle.put(lane)
+
+    def _run_on(self, prepared, lane):
+        if not prepared.items:
+            return np.empty((0, 0)), np.empty((0, 2)), {"graph_miss": False}
+        key = self._graph_key(prepared)
+        shape = key[:3]
+        self._check_items(prepared, shape)
+        slot, miss, build_ms = self._slot(prepared, key, lane)
+        logits, act = self._run_slot(slot, key, prepared, lane)
+        count = len(prepared.items)
+        return logits[:count].copy(), act[:count].copy(), {
+            "graph_miss": miss, "graph_build_ms": build_ms if miss else 0.0, "shape": list(shape),
+            "backend": self.backend, "precision": self.precision, "device": f"cuda:{self.device}"}
 
     def predict(self, state, questions):
         start = time.perf_counter()
@@ -283,12 +338,22 @@ class B200Engine:
         with self.lock:
             if self.closed:
                 return
-            self.graphs.clear()
-            getattr(self, "_io", {}).clear()
+            lanes = getattr(self, "_lanes", [self])
+            idle = getattr(self, "_idle", None)
+            if idle is not None:  # wait for every lane to be idle
+                held = [idle.get() for _ in lanes]
+            self.closed = True
+            for lane in lanes:
+                lane.graphs.clear()
+                getattr(lane, "_io", {}).clear()
+            for lane in lanes[1:]:  # lanes before the weights' owner
+                lane.native.close()
             if getattr(self, "native", None) is not None:
                 self.native.close()
             self.native = None
-            self.closed = True
+            if idle is not None:
+                for lane in held:
+                    idle.put(lane)
 
     def __enter__(self):
         return self

@@ -196,3 +196,46 @@ def test_run_packs_into_kept_host_arrays_like_fill():
         got = engine.native.seen[-1]
         for name in want:
             assert np.array_equal(got[name], want[name]), name
+
+
+def test_lanes_serve_concurrent_callers():
+    """With two lanes, two callers run at the same time, each on its own lane
+    (own native handle and graph slots); a third caller waits for an idle lane;
+    close() waits for the lanes and later calls raise."""
+    import queue
+    from laya_b200.engine import _Lane
+
+    class SlowNative(FakeNative):
+        def __init__(self, gate):
+            super().__init__()
+            self.gate = gate
+
+        def run(self, slot, inputs):
+            self.gate.wait(5)
+            return super().run(slot, inputs)
+
+    gate = threading.Event()
+    engine = make_engine(max_questions=4)
+    engine.native = SlowNative(gate)
+    engine._lanes = [engine, _Lane(SlowNative(gate))]
+    engine._idle = queue.Queue()
+    for lane in engine._lanes:
+        engine._idle.put(lane)
+    prepared = request_from_items(synthetic_items([30], ["noul"], seed=2, vocab=1000))
+    results = []
+    threads = [threading.Thread(target=lambda: results.append(engine.run_prepared(prepared))) for _ in range(3)]
+    for t in threads:
+        t.start()
+    import time
+    time.sleep(0.2)
+    assert engine._idle.qsize() == 0          # both lanes busy, the third caller waits
+    gate.set()
+    for t in threads:
+        t.join(5)
+    assert len(results) == 3
+    assert engine.native.runs + engine._lanes[1].native.runs == 3
+    assert engine.native.runs >= 1 and engine._lanes[1].native.runs >= 1
+    assert engine.graphs and engine._lanes[1].graphs  # each lane captured its own slot
+    engine.close()
+    with pytest.raises(RuntimeError, match="closed"):
+        engine.run_prepared(prepared)

@@ -144,3 +144,33 @@ def test_nvfp4_long_question_matches_nvfp4_oracle():
     compare(logits, act, ol, oa, inp["marker_mask"], TOL["nvfp4"], "nvfp4 C3 vs nvfp4 oracle")
     bl, _ = oracle_for(name, "bf16").forward(**inp)
     print(f"nvfp4 decision agreement with the bf16 oracle: {O.decision_agreement(bl, logits, inp['marker_mask']):.3f}")
+
+
+def test_serving_lanes_run_concurrently_with_identical_results():
+    """Two serving lanes (shared weights, own streams and graphs) serve two
+    callers at once; every result is bit-identical to a single-lane run, and
+    both lanes did work."""
+    import threading
+    from laya_b200.engine import B200Engine, request_from_items
+    for name in list(_ENGINES):
+        _ENGINES.pop(name).close()
+    items = [synthetic_items([64], ["noul"], seed=s, vocab=TINY.vocab) for s in range(6)]
+    with B200Engine(config=TINY, weights=weights_for("tiny"), device=0, max_questions=2, max_options=4,
+                    lanes=1) as one:
+        want = [one.run_prepared(request_from_items(it))[:2] for it in items]
+    with B200Engine(config=TINY, weights=weights_for("tiny"), device=0, max_questions=2, max_options=4,
+                    lanes=2) as eng:
+        got = [None] * len(items)
+
+        def worker(idx):
+            for i in idx:
+                got[i] = eng.run_prepared(request_from_items(items[i]))[:2]
+
+        threads = [threading.Thread(target=worker, args=(range(j, len(items), 2),)) for j in range(2)]
+        for t in threads:
+            t.start()
+        for t in threads:
+            t.join(120)
+        assert all(len(lane.graphs) > 0 for lane in eng._lanes)
+    for (wl, wa), (gl, ga) in zip(want, got):
+        assert np.array_equal(wl, gl) and np.array_equal(wa, ga)
