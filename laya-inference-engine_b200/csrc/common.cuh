@@ -276,6 +276,22 @@ DEVI float div_rn_by(float x, float d, float inv) {
   return fmaf(fmaf(-q, d, x), inv, q);
 }
 
+// Value of a non-negative e4m3 code (sign bit clear; 4 exponent bits, bias 7,
+// 3 mantissa bits), built from its bits: subnormals m * 2^-9, normals
+// (1 + m/8) * 2^(e-7) as an fp32 with exponent e + 120.
+DEVI float e4m3_value(uint32_t code) {
+  const uint32_t e = (code >> 3) & 0xF, m = code & 7;
+  return e == 0 ? (float)m * 0.001953125f : __uint_as_float(((e + 120u) << 23) | (m << 20));
+}
+
+// NVFP4 scale-block byte offset of (row, 16-element block g): blocks of
+// `rows_per_block` rows x 4 scale columns (512 bytes, byte (r%32)*16 + (r/32)*4
+// + g%4), the layout tcgen05.cp.32x128b.warpx4 moves into TMEM.
+DEVI size_t sf_offset(int row, int g, int rows_per_block, int col_blocks) {
+  const int rb = row / rows_per_block, r = row % rows_per_block;
+  return ((size_t)rb * col_blocks + (g >> 2)) * 512 + (r & 31) * 16 + (r >> 5) * 4 + (g & 3);
+}
+
 DEVI float warp_sum(float v) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);

@@ -478,18 +478,36 @@ struct Fwd {
 
   // NVFP4 projection: quantise the bf16 operand per row (scale blocks laid
   // out for the GEMM's token tile), then the block-scaled GEMM.
-  bool gemm_nv4(const Proj& w, const __nv_bfloat16* x, int M, int epi, __nv_bfloat16* out, int ldo, float* resid,
-                int ldr, const float* rope_cos = nullptr, const float* rope_sin = nullptr, int rope_seq = 0) {
-    const int kb = (w.K + 255) / 256;
-    int bn = 0, split = 1;
-    gemm_plan(M, w.N, kb, e->sm_count, &bn, &split);
-    if (bn > 128) {
-      bn = 128;
-      const int tiles = (w.N / 128) * ((M + bn - 1) / bn);
-      split = gemm_split(tiles, kb, e->sm_count, 8);
+  // Token tile, split-K and K blocks of an NVFP4 projection.
+  void nv4_plan(const Proj& w, int M, int* bn, int* split, int* kb) const {
+    *kb = (w.K + 255) / 256;
+    gemm_plan(M, w.N, *kb, e->sm_count, bn, split);
+    if (*bn > 128) {
+      *bn = 128;
+      const int tiles = (w.N / 128) * ((M + *bn - 1) / *bn);
+      *split = gemm_split(tiles, *kb, e->sm_count, 8);
     }
+  }
+
+  // NVFP4 output of a LayerNorm feeding projection w (M token rows).
+  void nv4_norm_out(NormParams& p, const Proj& w, int M) const {
+    int bn = 0, split = 1, kb = 0;
+    nv4_plan(w, M, &bn, &split, &kb);
+    p.out_x4 = e->x4;
+    p.out_x4_sf = e->x4sf;
+    p.out_x4_outer = e->x4o;
+    p.x4_rows_per_block = bn;
+    p.x4_col_blocks = 4 * kb;
+  }
+
+  // `quantized`: the LayerNorm before it already wrote the NVFP4 operand.
+  bool gemm_nv4(const Proj& w, const __nv_bfloat16* x, int M, int epi, __nv_bfloat16* out, int ldo, float* resid,
+                int ldr, const float* rope_cos = nullptr, const float* rope_sin = nullptr, int rope_seq = 0,
+                bool quantized = false) {
+    int bn = 0, split = 1, kb = 0;
+    nv4_plan(w, M, &bn, &split, &kb);
     const bool wide = split == 1 && bn >= 128;
-    if (on(kCatQuant)) {
+    if (on(kCatQuant) && !quantized) {
       QuantParams q{};
       q.rows = M;
       q.k = w.K;
@@ -580,13 +598,16 @@ struct Fwd {
       if (fp8) {
         p.out_fp8 = E.n8;
         p.out_fp8_scale = E.n8s;
+      } else if (nv4 && c.layers > 0) {
+        nv4_norm_out(p, E.wqkv[0], T);
       } else {
         p.out_bf16 = E.n;
       }
       norm(p);
     }
-    // LayerNorm feeding an encoder projection: bf16, or e4m3 + row scales.
-    auto enc_norm = [&](const std::string& wname) {
+    // LayerNorm feeding the encoder projection w: bf16, e4m3 + row scales, or
+    // the NVFP4 operand laid out for w's token tile.
+    auto enc_norm = [&](const std::string& wname, const Proj& w) {
       NormParams p{};
       p.rows = T;
       p.src = E.h;
@@ -595,6 +616,8 @@ struct Fwd {
       if (fp8) {
         p.out_fp8 = E.n8;
         p.out_fp8_scale = E.n8s;
+      } else if (nv4) {
+        nv4_norm_out(p, w, T);
       } else {
         p.out_bf16 = E.n;
       }
@@ -636,7 +659,7 @@ struct Fwd {
       if (short_bf16 && i > 0)
         gemm_ln(E.wqkv[i], wptr<float>(e, pre + "attn_norm.w"), T, kEpiStore, E.qkv, 3 * d, rc, rs, s);
       else
-        rotated = nv4 ? gemm_nv4(E.wqkv[i], E.n, T, kEpiStore, E.qkv, 3 * d, nullptr, 0, rc, rs, s)
+        rotated = nv4 ? gemm_nv4(E.wqkv[i], E.n, T, kEpiStore, E.qkv, 3 * d, nullptr, 0, rc, rs, s, true)
                       : gemm(E.wqkv[i], fp8 ? (const void*)E.n8 : (const void*)E.n, E.n8s, T, kEpiStore, E.qkv,
                              3 * d, nullptr, 0, rc, rs, s);
       AttnParams a{};
@@ -672,9 +695,9 @@ struct Fwd {
       if (short_bf16)
         gemm_ln(E.wi[i], wptr<float>(e, pre + "mlp_norm.w"), T, kEpiGeglu, E.g, I);
       else {
-        norm(enc_norm(pre + "mlp_norm.w"));
+        norm(enc_norm(pre + "mlp_norm.w", E.wi[i]));
         if (nv4)
-          gemm_nv4(E.wi[i], E.n, T, kEpiGeglu, E.g, I, nullptr, 0);
+          gemm_nv4(E.wi[i], E.n, T, kEpiGeglu, E.g, I, nullptr, 0, nullptr, nullptr, 0, true);
         else
           gemm(E.wi[i], fp8 ? (const void*)E.n8 : (const void*)E.n, E.n8s, T, kEpiGeglu, E.g, I, nullptr, 0);
       }
@@ -698,7 +721,7 @@ struct Fwd {
       if (last)
         norm(final_norm);
       else if (!short_bf16)
-        norm(enc_norm("enc." + std::to_string(i + 1) + ".attn_norm.w"));
+        norm(enc_norm("enc." + std::to_string(i + 1) + ".attn_norm.w", E.wqkv[i + 1]));
     }
     // Head layers (model.py:58-70): norm1 of layer j > 0 follows the previous
     // layer's linear2, norm2 follows out_proj.

@@ -203,11 +203,6 @@ __global__ void __launch_bounds__(BN >= 128 ? 256 : 128, BN == 128 ? 2 : 1)
 
 // ------------------------------------------------------------- quantisers
 
-// Scale-block byte offset of (row, scale column g) for row blocks of `rows_per_block`.
-DEVI size_t sf_offset(int row, int g, int rows_per_block, int col_blocks) {
-  const int rb = row / rows_per_block, r = row % rows_per_block;
-  return ((size_t)rb * col_blocks + (g >> 2)) * 512 + (r & 31) * 16 + (r >> 5) * 4 + (g & 3);
-}
 
 // One warp per row: 16-element blocks -> ue4m3 scale + 16 e2m1 nibbles.
 // outer > 0: fixed outer scale (weights, per tensor); outer <= 0: per-row
@@ -243,8 +238,7 @@ DEVI void nvfp4_row(const __nv_bfloat16* src, int k, float outer, float* row_out
     const float sc = fmaxf(bmax / (6.0f * outer), 0.001953125f);  // 2^-9 floor
     const uint8_t sc8 = (uint8_t)(f32x2_to_e4m3x2(sc, 0.f) & 0xFF);
     // decode the e4m3 scale exactly (1 sign, 4 exponent, 3 mantissa bits, bias 7)
-    const int ex = (sc8 >> 3) & 0xF, mt = sc8 & 7;
-    const float scale = ex == 0 ? ldexpf((float)mt, -9) : ldexpf(1.0f + mt / 8.0f, ex - 7);
+    const float scale = e4m3_value(sc8);
     const float denom = scale * outer;
     uint32_t w0 = 0, w1 = 0;
 #pragma unroll
@@ -321,8 +315,7 @@ __global__ void __launch_bounds__(256) quant_nvfp4_kernel(const QuantParams p, i
     if (c >= p.k) continue;
     const float sc = fmaxf(div_rn_by(bmax, o6, inv_o6), 0.001953125f);  // 2^-9 floor
     const uint8_t sc8 = (uint8_t)(f32x2_to_e4m3x2(sc, 0.f) & 0xFF);
-    const int ex = (sc8 >> 3) & 0xF, mt = sc8 & 7;
-    const float scale = ex == 0 ? ldexpf((float)mt, -9) : ldexpf(1.0f + mt / 8.0f, ex - 7);
+    const float scale = e4m3_value(sc8);
     const float denom = scale * outer, inv_d = 1.0f / denom;
     uint32_t w = 0;
 #pragma unroll
@@ -418,8 +411,8 @@ cudaError_t launch_quant_nvfp4(const QuantParams& p, int rows_per_block, int col
                      : p.k <= 3072 ? (const void*)quant_nvfp4_kernel<12>
                                    : (const void*)quant_nvfp4_kernel<16>;
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3((p.rows + 7) / 8, 1, 1);
-  cfg.blockDim = dim3(256, 1, 1);
+  cfg.gridDim = dim3((p.rows + 3) / 4, 1, 1);  // four rows per CTA (see launch_norm)
+  cfg.blockDim = dim3(128, 1, 1);
   cfg.stream = stream;
   cudaLaunchAttribute attr;
   attr.id = cudaLaunchAttributeProgrammaticStreamSerialization;

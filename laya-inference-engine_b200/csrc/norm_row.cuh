@@ -1,6 +1,6 @@
 // One LayerNorm row of the Laya forward (one warp, d = 128*NV fp32 values in
 // registers): the embedding gather, add_norm, the type-embedding add and an
-// optional second LayerNorm, with fp32 / bf16 / e4m3 outputs.
+// optional second LayerNorm, with fp32 / bf16 / e4m3 / NVFP4 outputs.
 //
 // Reference: add_norm and the embedding LN (src/laya_blackwell/model.py:15-19,
 // 84,90,97,102-104,59,68), _quantize_rows (quantization.py:20-29).  LayerNorm
@@ -67,7 +67,7 @@ DEVI void norm_row(const NormParams& p, int row, int lane) {
     for (int i = 0; i < NV; ++i) dst[lane + 32 * i] = x[i];
   }
   if (p.second_w) row_layernorm<NV>(x, p.d, p.eps, p.second_w, p.second_b, lane);
-  if (!p.out_bf16 && !p.out_fp8) return;
+  if (!p.out_bf16 && !p.out_fp8 && !p.out_x4) return;
   // bf16 of the row (also the FP8 quantiser's input, as in the reference where
   // _quantize_rows reads the bf16 normed activations).
   float amax = 0.f;
@@ -105,6 +105,31 @@ DEVI void norm_row(const NormParams& p, int row, int lane) {
       *reinterpret_cast<uint32_t*>(dst + (lane + 32 * i) * 4) = lo | (hi << 16);
     }
     if (lane == 0) p.out_fp8_scale[row] = scale;
+  }
+  if (p.out_x4) {
+    // NVFP4 (the activation quantiser's values): outer = max(amax/(6*448),
+    // 1e-20) per row; a 16-element block is 4 lanes' chunks, its e4m3 scale
+    // max(bmax/(6*outer), 2^-9), values e2m1(x / (scale*outer)).
+    amax = warp_max(amax);
+    const float outer = fmaxf(amax / (6.0f * 448.0f), 1e-20f);
+    if (lane == 0) p.out_x4_outer[row] = outer;
+    const float o6 = 6.0f * outer, inv_o6 = 1.0f / o6;
+    uint8_t* q = p.out_x4 + (size_t)row * (p.d / 2);
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+      float bmax = fmaxf(fmaxf(fabsf(x[i].x), fabsf(x[i].y)), fmaxf(fabsf(x[i].z), fabsf(x[i].w)));
+      bmax = fmaxf(bmax, __shfl_xor_sync(0xffffffffu, bmax, 1));
+      bmax = fmaxf(bmax, __shfl_xor_sync(0xffffffffu, bmax, 2));
+      const float sc = fmaxf(div_rn_by(bmax, o6, inv_o6), 0.001953125f);  // 2^-9 floor
+      const uint8_t sc8 = (uint8_t)(f32x2_to_e4m3x2(sc, 0.f) & 0xFF);
+      const float scale = e4m3_value(sc8);
+      const float denom = scale * outer, inv_d = 1.0f / denom;
+      const int col = (lane + 32 * i) * 4;
+      const uint32_t lo = f32x2_to_e2m1x2(div_rn_by(x[i].x, denom, inv_d), div_rn_by(x[i].y, denom, inv_d));
+      const uint32_t hi = f32x2_to_e2m1x2(div_rn_by(x[i].z, denom, inv_d), div_rn_by(x[i].w, denom, inv_d));
+      *reinterpret_cast<uint16_t*>(q + col / 2) = (uint16_t)(lo | (hi << 8));
+      if ((lane & 3) == 0) p.out_x4_sf[sf_offset(row, col / 16, p.x4_rows_per_block, p.x4_col_blocks)] = sc8;
+    }
   }
 }
 

@@ -42,6 +42,13 @@ struct NormParams {
   __nv_bfloat16* out_bf16;  // [rows][d] or null
   uint8_t* out_fp8;         // e4m3 per-row quantisation of the bf16 output, or null
   float* out_fp8_scale;     // [rows]
+  // NVFP4 quantisation of the bf16 output (per-row outer scale), laid out for
+  // a projection with `x4_rows_per_block`-token tiles, or null
+  uint8_t* out_x4;          // e2m1 [rows][d/2]
+  uint8_t* out_x4_sf;       // e4m3 block scales (tiled)
+  float* out_x4_outer;      // [rows]
+  int x4_rows_per_block;
+  int x4_col_blocks;
 };
 
 struct GemmParams {
