@@ -52,7 +52,7 @@ def parse():
     ap.add_argument("--precision", default="bf16", choices=["bf16", "fp8"])
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
     ap.add_argument("--lanes", type=int, default=2,
-                    help="c1: also time this many serving lanes replaying at once (1: skip)")
+                    help="c1 / c4: also time this many serving lanes working at once (1: skip)")
     ap.add_argument("--workload", default="c1", choices=["c1", "c2", "c3", "c4"],
                     help="c1 (default, the contract line): b=1 s=64 noul; c2: FP8 16x96; c3: NVFP4 1x512; "
                          "c4: FP8 64 questions s~U[32,512] bucketed by 32, sharded over ranks")
@@ -284,8 +284,9 @@ def run_batched(args):
     else:
         precision, buckets = "fp8", tuple(range(32, 513, 32))
         steps_items = [c4_step(300 + s, cfg.vocab) for s in range(4)]
+    lanes = max(1, args.lanes) if w == "c4" else 1   # C4 steps hold several bucket groups
     eng = B200Engine(config=cfg, device=local, precision=precision, max_questions=64, max_options=4,
-                     max_graphs=512, sequence_buckets=buckets)
+                     max_graphs=512, sequence_buckets=buckets, lanes=lanes)
     plans = []
     for items in steps_items:
         mine = shard_for_rank(items, world, rank, buckets) if world > 1 else list(range(len(items)))
@@ -293,7 +294,11 @@ def run_batched(args):
         plans.append([request_from_items([items[i] for i in idx]) for _, idx in groups])
     for plan in plans * max(1, args.warmup // len(plans)):     # captures every shape, then warm
         for req in plan:
-            eng.run_prepared(req)
+            eng._run_on(req, eng)
+    for lane in eng._lanes[1:]:                  # every lane holds every shape's graph
+        for plan in plans:
+            for req in plan:
+                eng._run_on(req, lane)
 
     def barrier():
         if dist:
@@ -312,7 +317,7 @@ def run_batched(args):
     for plan in plans:
         t = 0.0
         for req in plan:
-            eng.run_prepared(req)
+            eng._run_on(req, eng)                 # lane 0: its staging buffer now holds req
             slot = eng.graphs[eng._graph_key(req)]
             t += float(np.mean(eng.native.replay_device(slot, 5)))
         dev_ms.append(t)
@@ -324,6 +329,24 @@ def run_batched(args):
                 eng.run_prepared(req)
         wall = max_over_ranks(time.perf_counter() - t0)
         barrier()
+    # serving lanes (C4): the step's bucket groups dispatched concurrently, one
+    # caller thread per lane; host wall clock over the steps
+    lanes_line = None
+    if lanes > 1:
+        from concurrent.futures import ThreadPoolExecutor
+        with ThreadPoolExecutor(max_workers=lanes) as pool:
+            for plan in plans:
+                list(pool.map(eng.run_prepared, plan))
+            barrier()
+            t0 = time.perf_counter()
+            for k in range(args.steps):
+                list(pool.map(eng.run_prepared, plans[k % len(plans)]))
+            lanes_wall = max_over_ranks(time.perf_counter() - t0)
+            barrier()
+        lanes_line = {"lanes": lanes, "value": args.steps * sum(len(it) for it in steps_items) / len(steps_items)
+                      / lanes_wall, "unit": UNIT, "ms_per_step": 1000 * lanes_wall / args.steps,
+                      "timing": "host wall clock, bucket groups of a step on concurrent lanes (public API, "
+                                "host buffers)"}
     questions = sum(len(it) for it in steps_items) / len(steps_items)
     dev_step = max_over_ranks(float(np.mean(dev_ms)))
     value = questions / (dev_step / 1000.0)
@@ -346,6 +369,7 @@ def run_batched(args):
                              "frac": achieved / peak, "flops_per_step": flops,
                              "peak_source": f"{'2x' if precision == 'fp8' else '4x' if precision == 'nvfp4' else '1x'} "
                                             "measured cuBLAS bf16 (MEASURED_PEAKS.json)"},
+                **({"serving_lanes": lanes_line} if lanes_line else {}),
                 "clocks": cs}
         print(json.dumps(line), flush=True)
     eng.close()
@@ -372,7 +396,7 @@ def main():
                      max_graphs=2, lanes=max(1, args.lanes))
     items, inp = workload(cfg, seed=rank)
     prepared = request_from_items(items)
-    logits, act, meta = eng.run_prepared(prepared)  # captures the graph, inputs now resident
+    logits, act, meta = eng._run_on(prepared, eng)  # lane 0: captures the graph, inputs now resident
     slot = eng.graphs[(1, 64, 2, True)]
     native = eng.native
     kernels = native.kernel_count(slot)

@@ -239,6 +239,9 @@ struct laya_b200_engine {
   // enqueues the forward without a graph and synchronises after every
   // launch, so a device error names the launch that raised it.
   bool sync_check = false;
+  // The slot whose inputs the device staging buffer holds (set by run): a
+  // kernels-only replay of another slot would read another shape's layout.
+  int inputs_slot = -1;
 
   std::vector<cudaEvent_t> timing_events;
 };
@@ -1231,6 +1234,7 @@ int laya_b200_capture(laya_b200_engine* e, int batch, int seq, int options, int 
       if (!e->slots[i].live) {
         e->slots[i] = s;
         *slot = (int)i;
+        if (e->inputs_slot == (int)i) e->inputs_slot = -1;
         return;
       }
     e->slots.push_back(s);
@@ -1243,6 +1247,7 @@ int laya_b200_release(laya_b200_engine* e, int slot) {
     if (slot < 0 || slot >= (int)e->slots.size() || !e->slots[slot].live) fail("no slot %d", slot);
     ck(cudaStreamSynchronize(e->stream), "sync");
     free_slot(e->slots[slot]);
+    if (e->inputs_slot == slot) e->inputs_slot = -1;
   });
 }
 
@@ -1290,6 +1295,7 @@ int laya_b200_run(laya_b200_engine* e, int slot, const int64_t* input_ids, const
       ck(cudaGraphLaunch(sl.io_exec, e->stream), "graph launch");
     }
     ck(cudaStreamSynchronize(e->stream), "forward");
+    e->inputs_slot = slot;
     const uint32_t st = __atomic_load_n(e->status_host, __ATOMIC_ACQUIRE);
     if (st) {
       e->status_host[0] = 0;
@@ -1304,6 +1310,8 @@ int laya_b200_replay_device(laya_b200_engine* e, int slot, int iterations, int k
   return guard(e, [&] {
     if (slot < 0 || slot >= (int)e->slots.size() || !e->slots[slot].live) fail("no slot %d", slot);
     if (iterations < 1 || !ms_each || kernel_mask < 1 || kernel_mask > kCatAll) fail("bad arguments");
+    if (e->inputs_slot != slot)
+      fail("slot %d: the device inputs belong to another slot; run this slot once before replaying it", slot);
     Slot& sl = e->slots[slot];
     if (!sl.dev_exec[kernel_mask]) sl.dev_exec[kernel_mask] = capture_graph(e, sl.sh, kernel_mask, false, nullptr);
     while ((int)e->timing_events.size() < iterations + 1) {

@@ -174,3 +174,19 @@ def test_serving_lanes_run_concurrently_with_identical_results():
         assert all(len(lane.graphs) > 0 for lane in eng._lanes)
     for (wl, wa), (gl, ga) in zip(want, got):
         assert np.array_equal(wl, gl) and np.array_equal(wa, ga)
+
+
+def test_replay_refuses_a_slot_whose_inputs_are_not_resident():
+    """A kernels-only replay reads the device staging buffer with its own
+    shape's layout: after another slot ran, the engine refuses it (host-side
+    check, nothing is launched) until the slot runs again."""
+    nf = engine_for("tiny", "bf16")
+    a = nf.capture(1, 64, 2, False)
+    b = nf.capture(2, 64, 4, False)
+    nf.run(a, pack(synthetic_items([40], ["noul"], seed=1, vocab=TINY.vocab), 1, 64, 2, TINY.pad_token_id))
+    nf.replay_device(a, 2)
+    nf.run(b, pack(synthetic_items([40, 64], ["choice", "noul"], seed=2, vocab=TINY.vocab), 2, 64, 4,
+                   TINY.pad_token_id))
+    with pytest.raises(RuntimeError, match="another slot"):
+        nf.replay_device(a, 2)
+    nf.replay_device(b, 2)
