@@ -51,6 +51,8 @@ def parse():
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--precision", default="bf16", choices=["bf16", "fp8"])
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
+    ap.add_argument("--token-tables", action="store_true",
+                    help="c1: start each forward from the token tables (515 MB per GPU)")
     ap.add_argument("--lanes", type=int, default=2,
                     help="c1 / c4: also time this many serving lanes working at once (1: skip)")
     ap.add_argument("--workload", default="c1", choices=["c1", "c2", "c3", "c4"],
@@ -393,7 +395,7 @@ def main():
     from laya_b200.engine import B200Engine, request_from_items
     cfg = LAYA
     eng = B200Engine(config=cfg, device=local, precision=args.precision, max_questions=1, max_options=2,
-                     max_graphs=2, lanes=max(1, args.lanes))
+                     max_graphs=2, lanes=max(1, args.lanes), token_tables=args.token_tables)
     items, inp = workload(cfg, seed=rank)
     prepared = request_from_items(items)
     logits, act, meta = eng._run_on(prepared, eng)  # lane 0: captures the graph, inputs now resident
@@ -490,7 +492,8 @@ def main():
             "warmup": args.warmup, "ms_per_step": total_ms / args.steps, "p50_ms": p50,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": args.precision,
             "data": "synthetic (seeded token ids, seeded N(0,0.02) random-init weights of the 28x1024 Laya shape)",
-            "config": {"workload": "C1: one short noul question, b=1, s=64, k=2, warm CUDA-graph replay",
+            "config": {"workload": "C1: one short noul question, b=1, s=64, k=2, warm CUDA-graph replay"
+                                   + (", token tables" if args.token_tables else ""),
                        "model": "Laya: ModernBERT-large-shaped 28x1024 encoder + 2-layer head + scorer",
                        "global_batch": world, "seq_len": 64,
                        "parallelism": f"request-parallel replicas x{world} (no collective)",

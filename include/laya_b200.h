@@ -58,6 +58,16 @@ LAYA_B200_API int laya_b200_set_weight(laya_b200_engine* e, const char* name, co
  * scale) and build the weight tensor maps. */
 LAYA_B200_API int laya_b200_finalize(laya_b200_engine* e, int precision);
 
+/* Token tables (the reference fast mode's token_tables.py:13-38): compute,
+ * for every vocabulary id, the embedding LayerNorm row (fp32) and its layer-0
+ * QKV projection (bf16, before the rotary embedding) with the engine's own
+ * kernels and precision, so that a forward starts with one gather in place of
+ * the embedding norm and the layer-0 QKV projection.  Costs vocab * hidden *
+ * 10 bytes of device memory (515 MB for the Laya shape), shared with lanes
+ * created afterwards.  Call after finalize; slots captured before the call
+ * keep their old launch sequence. */
+LAYA_B200_API int laya_b200_build_token_tables(laya_b200_engine* e);
+
 /* Serving lanes (the multi-stream lanes of the reference's serving
  * experiments, experiments/latency/serving/README.md:6-14; no counterpart in
  * its engine API): a new engine handle on the parent's GPU that shares the

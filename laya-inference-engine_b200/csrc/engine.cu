@@ -179,6 +179,8 @@ struct WeightShare {
   int refs = 1;
   uint8_t* warena = nullptr;
   uint8_t* qarena = nullptr;
+  float* table_h = nullptr;             // token tables (optional)
+  __nv_bfloat16* table_qkv = nullptr;
 };
 
 }  // namespace
@@ -199,6 +201,10 @@ struct laya_b200_engine {
   uint8_t* qarena = nullptr;  // packed low-precision encoder weights
   size_t qarena_bytes = 0;
   WeightShare* weights = nullptr;  // owner of warena / qarena (shared with lanes)
+  // token tables: embedding LayerNorm rows [vocab][d] and layer-0 QKV rows
+  // [vocab][3d] (before the rotary embedding), or null
+  float* table_h = nullptr;
+  __nv_bfloat16* table_qkv = nullptr;
 
   // activations
   uint8_t* aarena = nullptr;
@@ -571,6 +577,36 @@ struct Fwd {
     count(launch_attention(p, batch, heads, st, pdl()), "attention launch");
   }
 
+  // Token-table rows [v0, v0 + n): the embedding LayerNorm of those ids and
+  // their layer-0 QKV projection (no rotary embedding), with the precision's
+  // own operand path, into E.h / E.qkv rows [0, n).
+  void token_table_rows(const int* iota, int v0, int n) {
+    laya_b200_engine& E = *e;
+    const bool fp8 = E.precision == LAYA_B200_FP8, nv4 = E.precision == LAYA_B200_NVFP4;
+    const int d = E.cfg.hidden;
+    NormParams p{};
+    p.rows = n;
+    p.tok_ids = iota + v0;
+    p.src = wptr<float>(e, "embed.tok");
+    p.ld_src = d;
+    p.w = wptr<float>(e, "embed.norm.w");
+    p.out_f32 = E.h;
+    p.ld_out_f32 = d;
+    if (fp8) {
+      p.out_fp8 = E.n8;
+      p.out_fp8_scale = E.n8s;
+    } else if (nv4) {
+      nv4_norm_out(p, E.wqkv[0], n);
+    } else {
+      p.out_bf16 = E.n;
+    }
+    norm(p);
+    if (nv4)
+      gemm_nv4(E.wqkv[0], E.n, n, kEpiStore, E.qkv, 3 * d, nullptr, 0, nullptr, nullptr, 0, true);
+    else
+      gemm(E.wqkv[0], fp8 ? (const void*)E.n8 : (const void*)E.n, E.n8s, n, kEpiStore, E.qkv, 3 * d, nullptr, 0);
+  }
+
   void run(const Shape& sh) {
     laya_b200_engine& E = *e;
     const laya_b200_config& c = E.cfg;
@@ -588,8 +624,26 @@ struct Fwd {
     const int* selpos = in + L.selpos;
     const int* score_rows = in + L.score;
 
+    // Token tables: one gather gives h and the rotated layer-0 qkv.
+    const bool tables = E.table_h != nullptr && c.layers > 0;
+    if (tables && on(kCatRows)) {
+      TokenGatherParams g{};
+      g.rows = T;
+      g.seq = s;
+      g.d = d;
+      g.ids = ids;
+      g.table_h = E.table_h;
+      g.table_qkv = E.table_qkv;
+      g.cos = E.gcos;
+      g.sin = E.gsin;
+      g.h = E.h;
+      g.ldh = d;
+      g.qkv = E.qkv;
+      g.ldqkv = 3 * d;
+      count(launch_token_gather(g, st, pdl()), "token gather launch");
+    }
     // enc.embeddings: gather + LayerNorm; layer 0 consumes bf16(h) (model.py:84,87-88)
-    {
+    if (!tables) {
       NormParams p{};
       p.rows = T;
       p.tok_ids = ids;
@@ -659,7 +713,9 @@ struct Fwd {
       const float* rs = glob ? E.gsin : E.lsin;
       // The rotary embedding runs in the projection's epilogue.
       bool rotated = true;
-      if (short_bf16 && i > 0)
+      if (tables && i == 0) {
+        // layer-0 qkv came from the token tables
+      } else if (short_bf16 && i > 0)
         gemm_ln(E.wqkv[i], wptr<float>(e, pre + "attn_norm.w"), T, kEpiStore, E.qkv, 3 * d, rc, rs, s);
       else
         rotated = nv4 ? gemm_nv4(E.wqkv[i], E.n, T, kEpiStore, E.qkv, 3 * d, nullptr, 0, rc, rs, s, true)
@@ -1055,6 +1111,8 @@ int laya_b200_create_lane(laya_b200_engine* parent, laya_b200_engine** out) {
     e->lin1 = parent->lin1;
     e->lin2 = parent->lin2;
     e->sc_fc1 = parent->sc_fc1;
+    e->table_h = parent->table_h;
+    e->table_qkv = parent->table_qkv;
     e->finalized = true;
     alloc_runtime(e.get());
   } catch (const Error& err) {
@@ -1064,6 +1122,49 @@ int laya_b200_create_lane(laya_b200_engine* parent, laya_b200_engine** out) {
   }
   *out = e.release();
   return 0;
+}
+
+int laya_b200_build_token_tables(laya_b200_engine* e) {
+  return guard(e, [&] {
+    if (!e->finalized) fail("finalize the weights before building token tables");
+    if (e->table_h) return;
+    const laya_b200_config& c = e->cfg;
+    if (c.layers < 1) fail("token tables need an encoder layer");
+    const size_t V = (size_t)c.vocab, d = (size_t)c.hidden;
+    WeightShare* w = e->weights;
+    ck(cudaMalloc(&w->table_h, V * d * 4), "token table (norm rows)");
+    ck(cudaMalloc(&w->table_qkv, V * 3 * d * 2), "token table (qkv rows)");
+    std::vector<int> iota(V);
+    for (size_t v = 0; v < V; ++v) iota[v] = (int)v;
+    int* d_iota = nullptr;
+    ck(cudaMalloc(&d_iota, V * 4), "token table ids");
+    try {
+      ck(cudaMemcpy(d_iota, iota.data(), V * 4, cudaMemcpyHostToDevice), "token table ids");
+      const int chunk = e->max_tokens;
+      for (size_t v0 = 0; v0 < V; v0 += chunk) {
+        const int n = (int)std::min((size_t)chunk, V - v0);
+        Fwd f{e, e->stream, kCatAll};
+        f.token_table_rows(d_iota, (int)v0, n);
+        ck(cudaMemcpyAsync(w->table_h + v0 * d, e->h, (size_t)n * d * 4, cudaMemcpyDeviceToDevice, e->stream),
+           "token table copy");
+        ck(cudaMemcpyAsync(w->table_qkv + v0 * 3 * d, e->qkv, (size_t)n * 3 * d * 2, cudaMemcpyDeviceToDevice,
+                           e->stream),
+           "token table copy");
+      }
+      ck(cudaStreamSynchronize(e->stream), "token tables");
+    } catch (...) {
+      cudaFree(d_iota);
+      throw;
+    }
+    cudaFree(d_iota);
+    if (e->status_host[0]) {
+      e->status_host[0] = 0;
+      fail("a device-side wait timed out while building the token tables");
+    }
+    e->table_h = w->table_h;
+    e->table_qkv = w->table_qkv;
+    e->inputs_slot = -1;  // the staging buffers were used for the tables
+  });
 }
 
 int laya_b200_set_weight(laya_b200_engine* e, const char* name, const void* host, size_t bytes) {
@@ -1395,6 +1496,8 @@ int laya_b200_destroy(laya_b200_engine* e) {
     if (left == 0) {
       cudaFree(e->weights->warena);
       cudaFree(e->weights->qarena);
+      cudaFree(e->weights->table_h);
+      cudaFree(e->weights->table_qkv);
       delete e->weights;
     }
   }

@@ -39,6 +39,7 @@ cudaError_t launch_quant_fp8(const QuantParams& p, cudaStream_t stream, bool pdl
 cudaError_t launch_gather_rows(float* dst, const float* src, const int* map, int rows, int d, cudaStream_t stream,
                                bool pdl);
 cudaError_t launch_tail(const TailParams& p, int batch, cudaStream_t stream, bool pdl);
+cudaError_t launch_token_gather(const TokenGatherParams& p, cudaStream_t stream, bool pdl);
 cudaError_t launch_pack_fp8_rows(const __nv_bfloat16* w, uint8_t* q, float* scale, int rows, int k,
                                  cudaStream_t stream);
 

@@ -98,6 +98,22 @@ struct LnParams {
 };
 
 
+// Forward start from the token tables (token_tables.cu).
+struct TokenGatherParams {
+  int rows;                        // tokens
+  int seq;                         // tokens per sequence (position = row % seq)
+  int d;
+  const int* ids;                  // [rows]
+  const float* table_h;            // [vocab][d] embedding LayerNorm rows
+  const __nv_bfloat16* table_qkv;  // [vocab][3d] layer-0 QKV rows, q / k not rotated
+  const float* cos;                // [max_len][64] global rotary tables
+  const float* sin;
+  float* h;                        // [rows][ldh]
+  int ldh;
+  __nv_bfloat16* qkv;              // [rows][ldqkv]
+  int ldqkv;
+};
+
 struct AttnParams {
   const __nv_bfloat16* qkv;  // [tokens][ld_qkv]; q at col h*64, k at d + h*64, v at 2d + h*64
   int ld_qkv;

@@ -13,6 +13,7 @@ LIB_PATH = Path(__file__).resolve().with_name("liblaya_b200.so")
 PRECISIONS = {"bf16": 0, "fp8": 1, "nvfp4": 2}
 
 EXPORTS = ("laya_b200_create", "laya_b200_set_weight", "laya_b200_finalize", "laya_b200_create_lane",
+           "laya_b200_build_token_tables",
            "laya_b200_capture",
            "laya_b200_release", "laya_b200_run", "laya_b200_replay_device", "laya_b200_kernel_count",
            "laya_b200_read_buffer", "laya_b200_tail_noalloc", "laya_b200_last_error", "laya_b200_destroy")
@@ -59,6 +60,7 @@ def load():
     sig = {
         "laya_b200_create": (I, [I, ctypes.POINTER(Config), ctypes.POINTER(P)]),
         "laya_b200_create_lane": (I, [P, ctypes.POINTER(P)]),
+        "laya_b200_build_token_tables": (I, [P]),
         "laya_b200_set_weight": (I, [P, ctypes.c_char_p, P, ctypes.c_size_t]),
         "laya_b200_finalize": (I, [P, I]),
         "laya_b200_capture": (I, [P, I, I, I, I, ctypes.POINTER(I)]),

@@ -121,6 +121,11 @@ class NativeForward:
         _lib.check(self.lib, self.handle, st, f"read_buffer({name})")
         return out
 
+    def build_token_tables(self):
+        """Embedding-norm and layer-0 QKV rows of every token id on the device
+        (slots captured afterwards start with one gather)."""
+        _lib.check(self.lib, self.handle, self.lib.laya_b200_build_token_tables(self.handle), "build_token_tables")
+
     def lane(self):
         """A serving lane: another handle on the same GPU sharing these
         weights, with its own stream, activations and graphs."""
@@ -156,7 +161,7 @@ class B200Engine:
     def __init__(self, model=None, *, weights=None, config: LayaConfig = LAYA, seed=0, device="cuda:0",
                  max_graphs=8, max_questions=64, sequence_buckets=(64, 128, 256, 384, 512, 768, 1024),
                  precision="bf16", max_options=256, tokenizer=None, agent_cfg=None, temperature=None,
-                 temperature_by_options=None, lanes=1):
+                 temperature_by_options=None, lanes=1, token_tables=False):
         if max_graphs < 1 or max_questions < 1:
             raise ValueError("max_graphs and max_questions must be positive")
         if lanes < 1:
@@ -183,6 +188,12 @@ class B200Engine:
         self.native = NativeForward(self.device, config, weights, precision, max_batch=max_questions,
                                     max_options=max_options)
         self.max_options = max_options
+        if token_tables:  # before the lanes, which share them
+            try:
+                self.native.build_token_tables()
+            except Exception:
+                self.native.close()
+                raise
         # Serving lanes: requests from concurrent callers run on idle lanes
         # (lane 0 is this object's own native / graphs); one lane serialises
         # every call like the reference's engine lock (engine.py:84,192).

@@ -255,3 +255,33 @@ def test_nvfp4_activation_quantiser_is_bit_exact(intermediate):
     deq = torch.from_numpy(vals).view(T, K // 16, 16) * scale[:, :, None]
     ref = ref_deq.view(T, K // 16, 16)
     assert torch.equal(deq, ref), int((deq != ref).sum())
+
+
+@pytest.mark.parametrize("precision,b", [("bf16", 1), ("bf16", 2), ("fp8", 2), ("nvfp4", 2)])
+def test_token_tables_match_the_computed_start(precision, b):
+    """Token tables (embedding-norm and layer-0 QKV rows per id, token_tables.py
+    of the reference's fast mode): the forward that starts from one gather
+    matches the oracle and the forward without tables, with one launch fewer
+    (gather in place of the embedding norm and the layer-0 QKV projection)."""
+    from laya_b200.engine import NativeForward
+    cfg = MICRO_LOCAL
+    w = seeded_weights(cfg, seed=10)
+    items = synthetic_items([64, 40][:b], ["choice", "noul"][:b], seed=23, vocab=cfg.vocab)
+    inp = pack(items, b, 64, 4, cfg.pad_token_id)
+    results = {}
+    for tables in (False, True):
+        nf = NativeForward(0, cfg, w, precision, max_batch=4, max_options=8)
+        try:
+            if tables:
+                nf.build_token_tables()
+            slot = nf.capture(b, 64, 4, b == 1)
+            results[tables] = nf.run(slot, inp) + (nf.kernel_count(slot),)
+        finally:
+            nf.close()
+    mm = inp["marker_mask"]
+    tol = {"bf16": 2e-2, "fp8": 6e-2, "nvfp4": 1.5e-1}[precision]
+    ol, oa = O.Oracle(w, cfg, precision).forward(**inp)
+    (l0, a0, k0), (l1, a1, k1) = results[False], results[True]
+    assert np.abs(l1[mm] - ol[mm]).max() <= tol and np.abs(a1 - oa).max() <= tol
+    assert np.abs(l1[mm] - l0[mm]).max() <= tol
+    assert k1 == k0 - 1
