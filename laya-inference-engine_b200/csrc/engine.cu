@@ -1,6 +1,8 @@
 // Host runtime behind the C ABI (include/laya_b200.h): weight arena and
-// packing, activation arena, per-shape CUDA-graph slots with pinned I/O, and
-// the forward's launch sequence.
+// packing, activation arena, per-shape CUDA-graph slots with pinned I/O,
+// serving lanes sharing the weights, token tables, and the forward's launch
+// sequence (with the batch-1 fusions: attention inside Wo, LayerNorm applied
+// on load by QKV / Wi).
 //
 // The forward mirrors FastDecisionModel.forward
 // (src/laya_blackwell/model.py:72-123); the slot / fill / replay logic mirrors

@@ -11,15 +11,17 @@
 // Pipeline per CTA: thread 0 issues TMA loads (weights first, before the
 // programmatic-dependent-launch wait, because weights never depend on the
 // previous kernel), thread 32 issues tcgen05.mma into a TMEM accumulator,
-// then all 128 threads move the accumulator to shared memory.
+// then the epilogue threads move the accumulator out of TMEM.
 //
 // Split-K: a thread-block cluster of S CTAs shares one output tile, each CTA
-// reducing a slice of K.  After the MMAs every CTA parks its fp32 partial in
-// its own shared memory; CTA r then sums rows {j, j+64 : j in its share} over
-// all S partials through distributed shared memory in rank order 0..S-1, so
-// the result is deterministic and no global workspace is needed.  The same
+// reducing a slice of K.  After the MMAs every CTA parks its fp32 partial in an
+// L2 scratch (or, when none is given, its own shared memory), the cluster
+// synchronises once, and CTA r sums rows {j, j+64 : j in its token share} over
+// all S partials in rank order 0..S-1, so the result is deterministic.  The
 // pairing of row j with row j+64 lets the GEGLU epilogue see act and gate of
-// one output column together (the packer interleaves Wi in blocks of 64).
+// one output column together (the packer interleaves Wi in blocks of 64); in
+// the QKV tiles rows j and j+32 pair instead, for the rotary embedding.
+// Unsplit 128-token tiles use the 256-thread wide epilogue with a TMA store.
 #include "common.cuh"
 #include "params.h"
 #include "launch.h"

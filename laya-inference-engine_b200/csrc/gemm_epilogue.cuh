@@ -1,6 +1,8 @@
-// Shared tail of the projection GEMMs (bf16, fp8 and nvfp4 mainloops): the
-// epilogue arithmetic and the split-K reduction of a 128-row x BN-token fp32
-// accumulator from TMEM across a thread-block cluster.
+// Shared tail of the projection kernels (bf16, fp8 and nvfp4 mainloops, the
+// fused attention and LayerNorm-on-load kernels): the epilogue arithmetic
+// (scales, bias, RoPE, activations, GEGLU, residual, LayerNorm statistics),
+// the split-K reduction of a 128-row x BN-token fp32 accumulator from TMEM
+// across a thread-block cluster, and the wide epilogue of unsplit tiles.
 #pragma once
 #include "common.cuh"
 #include "params.h"
@@ -139,9 +141,10 @@ DEVI void epilogue_rope(const GemmParams& p, int m, int n_lo, float4 lo, float4 
   *reinterpret_cast<uint2*>(o + n_hi) = *reinterpret_cast<uint2*>(oh);
 }
 
-// TMEM accumulator -> shared partial -> cluster reduction -> epilogue.
-// Called by all 128 threads after the MMA-done barrier completed.
-// `part` is this CTA's shared scratch of at least BN*128 floats (the
+// TMEM accumulator -> partial (L2 scratch p.partials, or the shared scratch
+// `part`) -> cluster reduction -> epilogue.  Called by all threads of the CTA
+// after the MMA-done barrier completed (threads 0-127 hold the TMEM lanes and
+// do the work).  `part` is at least BN*128 floats of shared memory (the
 // pipeline region, free once every MMA has completed).
 // LNST: residual epilogue that also writes the LayerNorm statistics of the
 // updated rows (p.ln_stats; bf16 projections without bias).
