@@ -270,23 +270,24 @@ __global__ void __launch_bounds__(256) nvfp4_pack_weight_kernel(const __nv_bfloa
   nvfp4_row(w + (size_t)row * k, k, outer, nullptr, q + (size_t)row * (k / 2), sf, row, 128, col_blocks, lane);
 }
 
-// Activation quantiser: one warp per row (k <= 256*MAXC), the same values as
-// nvfp4_row with a per-row outer scale.  The row is loaded into registers with
-// every load in flight at once; lane l holds elements [8l + 256i, +8), so a
-// 16-element block is split over a lane pair and its maximum takes one
-// shuffle; quotients use the FMA-corrected division (correctly rounded).
+// Activation quantiser: one CTA of 128 threads per row (k <= 1024*MAXC), the
+// same values as nvfp4_row with a per-row outer scale.  Each thread holds
+// elements [8t + 1024i, +8) in registers (every load in flight at once), so a
+// 16-element block is split over a thread pair and its maximum takes one
+// shuffle; the row maximum is a warp then CTA reduction; quotients use the
+// FMA-corrected division (correctly rounded).
 template <int MAXC>
-__global__ void __launch_bounds__(256) quant_nvfp4_kernel(const QuantParams p, int rows_per_block, int col_blocks) {
+__global__ void __launch_bounds__(128) quant_nvfp4_kernel(const QuantParams p, int rows_per_block, int col_blocks) {
+  __shared__ float s_max[4];
   griddep_launch_dependents();
   griddep_wait();
-  const int lane = threadIdx.x & 31;
-  const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int row = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   if (row >= p.rows) return;
   const __nv_bfloat16* src = p.src + (size_t)row * p.k;
   uint4 u[MAXC];
 #pragma unroll
   for (int i = 0; i < MAXC; ++i) {
-    const int c = lane * 8 + 256 * i;
+    const int c = tid * 8 + 1024 * i;
     u[i] = c < p.k ? *reinterpret_cast<const uint4*>(src + c) : make_uint4(0, 0, 0, 0);
   }
   float amax = 0.f;
@@ -297,13 +298,16 @@ __global__ void __launch_bounds__(256) quant_nvfp4_kernel(const QuantParams p, i
     for (int j = 0; j < 8; ++j) amax = fmaxf(amax, fabsf(__bfloat162float(e[j])));
   }
   amax = warp_max(amax);
+  if (lane == 0) s_max[warp] = amax;
+  __syncthreads();
+  amax = fmaxf(fmaxf(s_max[0], s_max[1]), fmaxf(s_max[2], s_max[3]));
   const float outer = fmaxf(amax / (6.0f * 448.0f), 1e-20f);
-  if (lane == 0) p.scale[row] = outer;
+  if (tid == 0) p.scale[row] = outer;
   const float o6 = 6.0f * outer, inv_o6 = 1.0f / o6;
   uint8_t* q = p.q + (size_t)row * (p.k / 2);
 #pragma unroll
   for (int i = 0; i < MAXC; ++i) {
-    const int c = lane * 8 + 256 * i;
+    const int c = tid * 8 + 1024 * i;
     const __nv_bfloat16* e = reinterpret_cast<const __nv_bfloat16*>(&u[i]);
     float x[8], bmax = 0.f;
 #pragma unroll
@@ -311,7 +315,7 @@ __global__ void __launch_bounds__(256) quant_nvfp4_kernel(const QuantParams p, i
       x[j] = __bfloat162float(e[j]);
       bmax = fmaxf(bmax, fabsf(x[j]));
     }
-    bmax = fmaxf(bmax, __shfl_xor_sync(0xffffffffu, bmax, 1));  // the lane pair of one 16-element block
+    bmax = fmaxf(bmax, __shfl_xor_sync(0xffffffffu, bmax, 1));  // the thread pair of one 16-element block
     if (c >= p.k) continue;
     const float sc = fmaxf(div_rn_by(bmax, o6, inv_o6), 0.001953125f);  // 2^-9 floor
     const uint8_t sc8 = (uint8_t)(f32x2_to_e4m3x2(sc, 0.f) & 0xFF);
@@ -322,7 +326,7 @@ __global__ void __launch_bounds__(256) quant_nvfp4_kernel(const QuantParams p, i
     for (int j = 0; j < 8; j += 2)
       w |= (uint32_t)f32x2_to_e2m1x2(div_rn_by(x[j], denom, inv_d), div_rn_by(x[j + 1], denom, inv_d)) << (4 * j);
     *reinterpret_cast<uint32_t*>(q + c / 2) = w;
-    if ((lane & 1) == 0) p.sf[sf_offset(row, c / 16, rows_per_block, col_blocks)] = sc8;
+    if ((tid & 1) == 0) p.sf[sf_offset(row, c / 16, rows_per_block, col_blocks)] = sc8;
   }
 }
 
@@ -406,12 +410,12 @@ cudaError_t launch_quant_nvfp4(const QuantParams& p, int rows_per_block, int col
   if (p.k % 16 || p.k > 4096) return cudaErrorInvalidValue;
   QuantParams q = p;
   void* args[] = {&q, &rows_per_block, &col_blocks};
-  const void* kern = p.k <= 1024   ? (const void*)quant_nvfp4_kernel<4>
-                     : p.k <= 2048 ? (const void*)quant_nvfp4_kernel<8>
-                     : p.k <= 3072 ? (const void*)quant_nvfp4_kernel<12>
-                                   : (const void*)quant_nvfp4_kernel<16>;
+  const void* kern = p.k <= 1024   ? (const void*)quant_nvfp4_kernel<1>
+                     : p.k <= 2048 ? (const void*)quant_nvfp4_kernel<2>
+                     : p.k <= 3072 ? (const void*)quant_nvfp4_kernel<3>
+                                   : (const void*)quant_nvfp4_kernel<4>;
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3((p.rows + 3) / 4, 1, 1);  // four rows per CTA (see launch_norm)
+  cfg.gridDim = dim3(p.rows, 1, 1);  // one CTA of 128 threads per row
   cfg.blockDim = dim3(128, 1, 1);
   cfg.stream = stream;
   cudaLaunchAttribute attr;

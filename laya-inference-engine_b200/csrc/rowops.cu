@@ -26,21 +26,23 @@ __global__ void __launch_bounds__(256) norm_kernel(const NormParams p) {
   norm_row<NV>(p, row, lane);
 }
 
-// Per-row e4m3 quantisation of a bf16 matrix (quantization.py:20-29).  The
-// warp's row (k <= 256*MAXC) is loaded into registers with all loads in
-// flight at once, so a short batch pays one memory latency, not one per chunk.
+// Per-row e4m3 quantisation of a bf16 matrix (quantization.py:20-29).  One
+// CTA of 128 threads per row (k <= 1024*MAXC): each thread holds its chunks of
+// 8 in registers with every load in flight at once, the row maximum is a warp
+// then CTA reduction, and quotients use the FMA-corrected division.  Four
+// warps per row keep a short batch's rows from being one long serial chain.
 template <int MAXC>
-__global__ void __launch_bounds__(256) quant_fp8_kernel(const QuantParams p) {
+__global__ void __launch_bounds__(128) quant_fp8_kernel(const QuantParams p) {
+  __shared__ float s_max[4];
   griddep_launch_dependents();
   griddep_wait();
-  const int lane = threadIdx.x & 31;
-  const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int row = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   if (row >= p.rows) return;
   const __nv_bfloat16* src = p.src + (size_t)row * p.k;
   uint4 u[MAXC];
 #pragma unroll
   for (int i = 0; i < MAXC; ++i) {
-    const int c = lane * 8 + 256 * i;
+    const int c = tid * 8 + 1024 * i;
     u[i] = c < p.k ? *reinterpret_cast<const uint4*>(src + c) : make_uint4(0, 0, 0, 0);
   }
   float amax = 0.f;
@@ -51,11 +53,14 @@ __global__ void __launch_bounds__(256) quant_fp8_kernel(const QuantParams p) {
     for (int j = 0; j < 8; ++j) amax = fmaxf(amax, fabsf(__bfloat162float(e[j])));
   }
   amax = warp_max(amax);
+  if (lane == 0) s_max[warp] = amax;
+  __syncthreads();
+  amax = fmaxf(fmaxf(s_max[0], s_max[1]), fmaxf(s_max[2], s_max[3]));
   const float scale = fmaxf(amax / 448.0f, 1e-12f), inv = 1.0f / scale;
   uint8_t* dst = p.q + (size_t)row * p.k;
 #pragma unroll
   for (int i = 0; i < MAXC; ++i) {
-    const int c = lane * 8 + 256 * i;
+    const int c = tid * 8 + 1024 * i;
     if (c >= p.k) continue;
     const __nv_bfloat16* e = reinterpret_cast<const __nv_bfloat16*>(&u[i]);
     uint32_t w[2];
@@ -69,7 +74,7 @@ __global__ void __launch_bounds__(256) quant_fp8_kernel(const QuantParams p) {
     }
     *reinterpret_cast<uint2*>(dst + c) = make_uint2(w[0], w[1]);
   }
-  if (lane == 0) p.scale[row] = scale;
+  if (tid == 0) p.scale[row] = scale;
 }
 
 // dst[r] = src[map[r]] for fp32 rows of width d (multiple of 4).
@@ -247,11 +252,20 @@ cudaError_t launch_quant_fp8(const QuantParams& p, cudaStream_t stream, bool pdl
   if (p.k % 8 || p.k > 4096) return cudaErrorInvalidValue;
   QuantParams q = p;
   void* args[] = {&q};
-  const void* kern = p.k <= 1024   ? (const void*)quant_fp8_kernel<4>
-                     : p.k <= 2048 ? (const void*)quant_fp8_kernel<8>
-                     : p.k <= 3072 ? (const void*)quant_fp8_kernel<12>
-                                   : (const void*)quant_fp8_kernel<16>;
-  return launch_rows(kern, args, p.rows, 0, stream, pdl);
+  const void* kern = p.k <= 1024   ? (const void*)quant_fp8_kernel<1>
+                     : p.k <= 2048 ? (const void*)quant_fp8_kernel<2>
+                     : p.k <= 3072 ? (const void*)quant_fp8_kernel<3>
+                                   : (const void*)quant_fp8_kernel<4>;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(p.rows, 1, 1);  // one CTA of 128 threads per row
+  cfg.blockDim = dim3(128, 1, 1);
+  cfg.stream = stream;
+  cudaLaunchAttribute attr;
+  attr.id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr.val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = &attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  return cudaLaunchKernelExC(&cfg, kern, args);
 }
 
 cudaError_t launch_gather_rows(float* dst, const float* src, const int* map, int rows, int d, cudaStream_t stream,
