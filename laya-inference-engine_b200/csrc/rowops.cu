@@ -26,6 +26,15 @@ __global__ void __launch_bounds__(256) norm_kernel(const NormParams p) {
   norm_row<NV>(p, row, lane);
 }
 
+// One CTA of d/8 threads per row (d a multiple of 256): see norm_row_cta.
+__global__ void __launch_bounds__(128) norm_cta_kernel(const NormParams p) {
+  __shared__ float red[4];
+  griddep_launch_dependents();
+  griddep_wait();
+  if ((int)blockIdx.x >= p.rows) return;
+  norm_row_cta(p, blockIdx.x, red);
+}
+
 // Per-row e4m3 quantisation of a bf16 matrix (quantization.py:20-29).  One
 // CTA of 128 threads per row (k <= 1024*MAXC): each thread holds its chunks of
 // 8 in registers with every load in flight at once, the row maximum is a warp
@@ -243,8 +252,19 @@ cudaError_t launch_norm(const NormParams& p, cudaStream_t stream, bool pdl) {
     case 7: kern = (const void*)norm_kernel<7>; break;
     case 8: kern = (const void*)norm_kernel<8>; break;
   }
-  // rows with NVFP4 output carry much more per-row work: four rows per CTA
-  // spread them over twice the SMs (measured 2.52 -> 2.45 ms per C3 forward)
+  if ((p.out_fp8 || p.out_x4) && p.d % 256 == 0) {
+    // quantised outputs carry much more per-row work: one CTA per row
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(p.rows, 1, 1);
+    cfg.blockDim = dim3(p.d / 8, 1, 1);
+    cfg.stream = stream;
+    cudaLaunchAttribute attr;
+    attr.id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr.val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = &attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    return cudaLaunchKernelExC(&cfg, (const void*)norm_cta_kernel, args);
+  }
   return launch_rows(kern, args, p.rows, 0, stream, pdl, p.out_x4 ? 4 : 8);
 }
 

@@ -285,3 +285,58 @@ def test_token_tables_match_the_computed_start(precision, b):
     assert np.abs(l1[mm] - ol[mm]).max() <= tol and np.abs(a1 - oa).max() <= tol
     assert np.abs(l1[mm] - l0[mm]).max() <= tol
     assert k1 == k0 - 1
+
+
+@pytest.mark.parametrize("precision", ["fp8", "nvfp4"])
+@pytest.mark.parametrize("hidden", [256, 768])
+def test_layernorm_quantised_outputs_match_oracle(precision, hidden):
+    """LayerNorm rows with a quantised output (add_norm, model.py:15-19, then
+    _quantize_rows / the NVFP4 quantiser) against the oracle.  Replaying only
+    the row kernels leaves the MLP norm of the embedding-norm output as the
+    last quantised operand.  The fp32 reduction order of the two LayerNorms
+    differs from the oracle's, so a few elements round to the neighbouring
+    bf16 value; everything else is identical."""
+    from laya_b200.engine import NativeForward
+    cfg = LayaConfig(layers=1, hidden=hidden, heads=hidden // 64, intermediate=384, vocab=1000, pad_token_id=999,
+                     max_len=512, head_layers=0, head_heads=hidden // 64, head_ff=512, act_hidden=64)
+    w = seeded_weights(cfg, seed=17)
+    nf = NativeForward(0, cfg, w, precision, max_batch=4, max_options=8)
+    try:
+        b, s, k = 2, 192, 4
+        items = synthetic_items([192, 100], ["choice", "noul"], seed=29, vocab=cfg.vocab)
+        inp = pack(items, b, s, k, cfg.pad_token_id)
+        slot = nf.capture(b, s, k, False)
+        nf.run(slot, inp)
+        nf.replay_device(slot, 1, kernel_mask=4)
+        T, d = b * s, hidden
+        if precision == "fp8":
+            q = torch.from_numpy(nf.read_buffer("n8", (T, d), np.uint8).copy()).view(torch.float8_e4m3fn)
+            scale = torch.from_numpy(nf.read_buffer("n8s", (T,), np.float32))
+        else:
+            nib = nf.read_buffer("x4", (T, d // 2), np.uint8)
+            outer = torch.from_numpy(nf.read_buffer("x4o", (T,), np.float32))
+    finally:
+        nf.close()
+    wf = {kk: torch.from_numpy(v) for kk, v in as_float32(w).items()}
+    ids = torch.from_numpy(inp["input_ids"]).reshape(-1)
+    h0 = O.layer_norm(wf["embed.tok"][ids], wf["embed.norm.w"], None, cfg.norm_eps)
+    n1 = O.bf16(O.layer_norm(h0, wf["enc.0.mlp_norm.w"], None, cfg.norm_eps))
+    if precision == "fp8":
+        q_ref, scale_ref = O.fp8_quantize_rows(n1)
+        assert float(((scale - scale_ref[:, 0]).abs() / scale_ref[:, 0]).max()) < 1e-2
+        assert float((scale != scale_ref[:, 0]).float().mean()) < 0.02
+        assert float((q.to(torch.float32) != q_ref).float().mean()) < 2e-3
+    else:
+        _, outer_ref = O.nvfp4_quantize(n1, per_row=True)
+        outer_ref = outer_ref[:, 0]
+        assert float(((outer - outer_ref).abs() / outer_ref).max()) < 1e-2
+        assert float((outer != outer_ref).float().mean()) < 0.02
+        # e2m1 codes against the oracle's, from its block scales
+        blocks = n1.reshape(T, d // 16, 16)
+        sc = O.e4m3(torch.clamp(blocks.abs().amax(dim=2, keepdim=True) / (6.0 * outer_ref[:, None, None]),
+                                min=2.0 ** -9))
+        v_ref = O.e2m1(blocks / (sc * outer_ref[:, None, None])).reshape(T, d)
+        codes = np.stack([nib & 0xF, nib >> 4], axis=-1).reshape(T, d)
+        grid = np.array([0.0, 0.5, 1.0, 1.5, 2.0, 3.0, 4.0, 6.0], np.float32)
+        v = torch.from_numpy(grid[codes & 7] * np.where(codes & 8, -1.0, 1.0).astype(np.float32))
+        assert float((v != v_ref).float().mean()) < 2e-3
