@@ -352,83 +352,112 @@ DEVI void tile_epilogue_wide(const GemmParams& p, const CUtensorMap* omap, uint3
     __syncthreads();
     return;
   }
-  for (int it = tid; it < items; it += THREADS) {
-    const int tok = it / quads, q = it % quads;
-    const int r0 = 4 * q;
-    float x[4], g[4];
-    {
-      const float4 a = *reinterpret_cast<const float4*>(P + tok * 128 + r0);
-      x[0] = a.x; x[1] = a.y; x[2] = a.z; x[3] = a.w;
-      if (ep == kEpiGeglu) {
-        const float4 b = *reinterpret_cast<const float4*>(P + tok * 128 + 64 + r0);
-        g[0] = b.x; g[1] = b.y; g[2] = b.z; g[3] = b.w;
+  // THREADS is a multiple of `quads`, so every item of a thread covers the
+  // same 4 rows: the per-row constants (weight scales, bias, the rotation
+  // partner) are loaded once, and the rotary tables of a thread's tokens are
+  // loaded in batches of KB tokens ahead of the arithmetic (a load per item
+  // left the loop latency-bound).
+  static_assert(THREADS % 32 == 0, "wide epilogue: whole warps");
+  const int q = tid % quads, r0 = 4 * q, n = tile_n * 128 + r0;
+  const int tok_step = THREADS / quads;
+  const bool rot = n < p.rope_cols;
+  const int d0 = r0 & 63, pr = d0 < 32 ? r0 + 32 : r0 - 32;
+  float wx[4] = {1.f, 1.f, 1.f, 1.f}, wg[4] = {1.f, 1.f, 1.f, 1.f}, wy[4] = {1.f, 1.f, 1.f, 1.f};
+  if (KIND == kKindFp8) {
+    const float4 a = *reinterpret_cast<const float4*>(p.w_scale + n);
+    wx[0] = a.x; wx[1] = a.y; wx[2] = a.z; wx[3] = a.w;
+    if (ep == kEpiGeglu) {
+      const float4 b = *reinterpret_cast<const float4*>(p.w_scale + n + 64);
+      wg[0] = b.x; wg[1] = b.y; wg[2] = b.z; wg[3] = b.w;
+    }
+    if (rot) {
+      const float4 c = *reinterpret_cast<const float4*>(p.w_scale + tile_n * 128 + pr);
+      wy[0] = c.x; wy[1] = c.y; wy[2] = c.z; wy[3] = c.w;
+    }
+  }
+  float bx[4] = {0.f, 0.f, 0.f, 0.f};
+  const bool has_bias = p.bias != nullptr && !rot && ep != kEpiGeglu;
+  if (has_bias) {
+    const uint2 bu = *reinterpret_cast<const uint2*>(p.bias + n);
+    const __nv_bfloat16* bb = reinterpret_cast<const __nv_bfloat16*>(&bu);
+#pragma unroll
+    for (int e = 0; e < 4; ++e) bx[e] = __bfloat162float(bb[e]);
+  }
+  constexpr int KB = 4;
+  for (int tb = tid / quads; tb < BN; tb += KB * tok_step) {
+    float4 cv[KB], sv[KB];
+    if (rot) {
+#pragma unroll
+      for (int u = 0; u < KB; ++u) {
+        const int tok = tb + u * tok_step;
+        const int pos = (m_base + (tok < BN ? tok : 0)) % p.rope_seq;
+        cv[u] = *reinterpret_cast<const float4*>(p.rope_cos + (size_t)pos * 64 + d0);
+        sv[u] = *reinterpret_cast<const float4*>(p.rope_sin + (size_t)pos * 64 + d0);
       }
     }
-    const int n = tile_n * 128 + r0;
-    if (KIND == kKindFp8) {
-      const float4 w = *reinterpret_cast<const float4*>(p.w_scale + n);
-      const float ww[4] = {w.x, w.y, w.z, w.w};
 #pragma unroll
-      for (int e = 0; e < 4; ++e) x[e] = (x[e] * S[tok]) * ww[e];
-      if (ep == kEpiGeglu) {
-        const float4 w2 = *reinterpret_cast<const float4*>(p.w_scale + n + 64);
-        const float wg[4] = {w2.x, w2.y, w2.z, w2.w};
-#pragma unroll
-        for (int e = 0; e < 4; ++e) g[e] = (g[e] * S[tok]) * wg[e];
+    for (int u = 0; u < KB; ++u) {
+      const int tok = tb + u * tok_step;
+      if (tok >= BN) break;
+      float x[4], g[4];
+      {
+        const float4 a = *reinterpret_cast<const float4*>(P + tok * 128 + r0);
+        x[0] = a.x; x[1] = a.y; x[2] = a.z; x[3] = a.w;
+        g[0] = g[1] = g[2] = g[3] = 0.f;
+        if (ep == kEpiGeglu) {
+          const float4 b = *reinterpret_cast<const float4*>(P + tok * 128 + 64 + r0);
+          g[0] = b.x; g[1] = b.y; g[2] = b.z; g[3] = b.w;
+        }
       }
-    } else if (KIND == kKindNvfp4) {
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        x[e] *= S[tok] * tsc;
-        g[e] *= S[tok] * tsc;
-      }
-    }
-    __nv_bfloat16 o[4];
-    if (n < p.rope_cols) {
-      // bf16(qkv) rotated in fp32 without FMA, as rope_qkv does (kernels.py:62-93)
-      const int d0 = r0 & 63;
-      const int pr = d0 < 32 ? r0 + 32 : r0 - 32;
-      const float4 pb = *reinterpret_cast<const float4*>(P + tok * 128 + pr);
-      float y[4] = {pb.x, pb.y, pb.z, pb.w};
       if (KIND == kKindFp8) {
-        const float4 w = *reinterpret_cast<const float4*>(p.w_scale + tile_n * 128 + pr);
-        const float ww[4] = {w.x, w.y, w.z, w.w};
 #pragma unroll
-        for (int e = 0; e < 4; ++e) y[e] = (y[e] * S[tok]) * ww[e];
+        for (int e = 0; e < 4; ++e) {
+          x[e] = (x[e] * S[tok]) * wx[e];
+          g[e] = (g[e] * S[tok]) * wg[e];
+        }
       } else if (KIND == kKindNvfp4) {
 #pragma unroll
-        for (int e = 0; e < 4; ++e) y[e] *= S[tok] * tsc;
+        for (int e = 0; e < 4; ++e) {
+          x[e] *= S[tok] * tsc;
+          g[e] *= S[tok] * tsc;
+        }
       }
-      const int pos = (m_base + tok) % p.rope_seq;
-      const float* cs = p.rope_cos + (size_t)pos * 64 + d0;
-      const float* sn = p.rope_sin + (size_t)pos * 64 + d0;
+      __nv_bfloat16 o[4];
+      if (rot) {
+        // bf16(qkv) rotated in fp32 without FMA, as rope_qkv does (kernels.py:62-93)
+        const float4 pb = *reinterpret_cast<const float4*>(P + tok * 128 + pr);
+        float y[4] = {pb.x, pb.y, pb.z, pb.w};
+        if (KIND == kKindFp8) {
 #pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const float a = bf16_round(x[e]), b = bf16_round(y[e]);
-        const float rot = __fmul_rn(d0 < 32 ? -b : b, sn[e]);
-        o[e] = __float2bfloat16_rn(__fadd_rn(__fmul_rn(a, cs[e]), rot));
+          for (int e = 0; e < 4; ++e) y[e] = (y[e] * S[tok]) * wy[e];
+        } else if (KIND == kKindNvfp4) {
+#pragma unroll
+          for (int e = 0; e < 4; ++e) y[e] *= S[tok] * tsc;
+        }
+        const float cs[4] = {cv[u].x, cv[u].y, cv[u].z, cv[u].w};
+        const float sn[4] = {sv[u].x, sv[u].y, sv[u].z, sv[u].w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float a = bf16_round(x[e]), b = bf16_round(y[e]);
+          const float rotp = __fmul_rn(d0 < 32 ? -b : b, sn[e]);
+          o[e] = __float2bfloat16_rn(__fadd_rn(__fmul_rn(a, cs[e]), rotp));
+        }
+        *reinterpret_cast<uint2*>(O + tok * 128 + r0) = *reinterpret_cast<uint2*>(o);
+      } else if (ep == kEpiGeglu) {
+#pragma unroll
+        for (int e = 0; e < 4; ++e)
+          o[e] = __float2bfloat16_rn(bf16_round(gelu_erf(bf16_round(x[e]))) * bf16_round(g[e]));
+        *reinterpret_cast<uint2*>(O + tok * 64 + r0) = *reinterpret_cast<uint2*>(o);
+      } else {
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          float y = has_bias ? x[e] + bx[e] : x[e];
+          if (ep == kEpiRelu) y = fmaxf(y, 0.f);
+          else if (ep == kEpiGelu) y = gelu_erf(bf16_round(y));
+          o[e] = __float2bfloat16_rn(y);
+        }
+        *reinterpret_cast<uint2*>(O + tok * 128 + r0) = *reinterpret_cast<uint2*>(o);
       }
-      *reinterpret_cast<uint2*>(O + tok * 128 + r0) = *reinterpret_cast<uint2*>(o);
-    } else if (ep == kEpiGeglu) {
-#pragma unroll
-      for (int e = 0; e < 4; ++e)
-        o[e] = __float2bfloat16_rn(bf16_round(gelu_erf(bf16_round(x[e]))) * bf16_round(g[e]));
-      *reinterpret_cast<uint2*>(O + tok * 64 + r0) = *reinterpret_cast<uint2*>(o);
-    } else {
-      if (p.bias) {
-        const uint2 bu = *reinterpret_cast<const uint2*>(p.bias + n);
-        const __nv_bfloat16* bb = reinterpret_cast<const __nv_bfloat16*>(&bu);
-#pragma unroll
-        for (int e = 0; e < 4; ++e) x[e] += __bfloat162float(bb[e]);
-      }
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        float y = x[e];
-        if (ep == kEpiRelu) y = fmaxf(y, 0.f);
-        else if (ep == kEpiGelu) y = gelu_erf(bf16_round(y));
-        o[e] = __float2bfloat16_rn(y);
-      }
-      *reinterpret_cast<uint2*>(O + tok * 128 + r0) = *reinterpret_cast<uint2*>(o);
     }
   }
   fence_proxy_async_smem();
