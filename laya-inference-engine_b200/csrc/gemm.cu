@@ -38,7 +38,8 @@ struct GemmCfg {
   static constexpr int B_BYTES = BN * 128;    // BN token rows x 128 bytes of K
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
   static constexpr int PIPE_BYTES = STAGES * STAGE_BYTES;
-  static constexpr int PART_BYTES = BN * 128 * 4;
+  // split-K partial, or the wide epilogue's fp32 tile + bf16 output + row scales
+  static constexpr int PART_BYTES = BN >= 128 ? BN * 128 * 4 + BN * 128 * 2 + BN * 4 : BN * 128 * 4;
   static constexpr int MAIN_BYTES = PIPE_BYTES > PART_BYTES ? PIPE_BYTES : PART_BYTES;
   static constexpr int BAR_BYTES = 256;
   static constexpr int SMEM = MAIN_BYTES + BAR_BYTES + 1024;

@@ -9,14 +9,42 @@
 
 namespace laya {
 
+// Global operands of one epilogue item that do not depend on the split-K
+// partials: the activation row scale, the residual rows (residual epilogues)
+// and the rotary table entries (rotary tiles).  Loaded together with the
+// partials so that an item costs one memory round trip.
+struct EpiPre {
+  float sa;
+  float4 ra, rb;          // residual rows n_lo.., n_lo+64..
+  float4 c0, c1, s0, s1;  // cos / sin at d0 and d0+32
+};
+
+template <int KIND>
+DEVI EpiPre epi_prefetch(const GemmParams& p, int m, int n_lo, bool residual, bool rope) {
+  EpiPre e;
+  e.sa = KIND == kKindBf16 ? 1.f : p.a_scale[m];
+  if (residual) {
+    e.ra = __ldcg(reinterpret_cast<const float4*>(p.resid + (size_t)m * p.ldr + n_lo));
+    e.rb = __ldcg(reinterpret_cast<const float4*>(p.resid + (size_t)m * p.ldr + n_lo + 64));
+  }
+  if (rope) {
+    const int pos = m % p.rope_seq, d0 = n_lo & 63;
+    e.c0 = *reinterpret_cast<const float4*>(p.rope_cos + (size_t)pos * 64 + d0);
+    e.c1 = *reinterpret_cast<const float4*>(p.rope_cos + (size_t)pos * 64 + d0 + 32);
+    e.s0 = *reinterpret_cast<const float4*>(p.rope_sin + (size_t)pos * 64 + d0);
+    e.s1 = *reinterpret_cast<const float4*>(p.rope_sin + (size_t)pos * 64 + d0 + 32);
+  }
+  return e;
+}
+
 // Epilogue for 4 consecutive weight rows n_lo..n_lo+3 and their partners
 // n_lo+64..n_lo+67 of one token m (lo/hi hold the fp32 accumulators).
 template <int KIND>
-DEVI void epilogue_quad(const GemmParams& p, int m, int n_lo, int geglu_col, float4 lo, float4 hi) {
+DEVI void epilogue_quad(const GemmParams& p, int m, int n_lo, int geglu_col, float4 lo, float4 hi, const EpiPre& pre) {
   float l[4] = {lo.x, lo.y, lo.z, lo.w}, h[4] = {hi.x, hi.y, hi.z, hi.w};
   const int n_hi = n_lo + 64;
   if (KIND == kKindFp8) {
-    const float sa = p.a_scale[m];
+    const float sa = pre.sa;
     const float4 wl = *reinterpret_cast<const float4*>(p.w_scale + n_lo);
     const float4 wh = *reinterpret_cast<const float4*>(p.w_scale + n_hi);
     const float wlv[4] = {wl.x, wl.y, wl.z, wl.w}, whv[4] = {wh.x, wh.y, wh.z, wh.w};
@@ -26,7 +54,7 @@ DEVI void epilogue_quad(const GemmParams& p, int m, int n_lo, int geglu_col, flo
       h[e] = (h[e] * sa) * whv[e];
     }
   } else if (KIND == kKindNvfp4) {
-    const float sa = p.a_scale[m] * p.w_tensor_scale;
+    const float sa = pre.sa * p.w_tensor_scale;
 #pragma unroll
     for (int e = 0; e < 4; ++e) {
       l[e] *= sa;
@@ -57,7 +85,7 @@ DEVI void epilogue_quad(const GemmParams& p, int m, int n_lo, int geglu_col, flo
   if (p.epilogue == kEpiResidual) {
     float4* rl = reinterpret_cast<float4*>(p.resid + (size_t)m * p.ldr + n_lo);
     float4* rh = reinterpret_cast<float4*>(p.resid + (size_t)m * p.ldr + n_hi);
-    float4 a = *rl, b = *rh;
+    float4 a = pre.ra, b = pre.rb;
     a.x += bf16_round(l[0]); a.y += bf16_round(l[1]); a.z += bf16_round(l[2]); a.w += bf16_round(l[3]);
     b.x += bf16_round(h[0]); b.y += bf16_round(h[1]); b.z += bf16_round(h[2]); b.w += bf16_round(h[3]);
     *rl = a;
@@ -90,11 +118,11 @@ DEVI void epilogue_quad(const GemmParams& p, int m, int n_lo, int geglu_col, flo
 // bf16(qkv) rotated in fp32 without FMA contraction, as rope_qkv does
 // (kernels.py:62-93), at the token's position m % rope_seq.
 template <int KIND>
-DEVI void epilogue_rope(const GemmParams& p, int m, int n_lo, float4 lo, float4 hi) {
+DEVI void epilogue_rope(const GemmParams& p, int m, int n_lo, float4 lo, float4 hi, const EpiPre& pre) {
   float l[4] = {lo.x, lo.y, lo.z, lo.w}, h[4] = {hi.x, hi.y, hi.z, hi.w};
   const int n_hi = n_lo + 32;
   if (KIND == kKindFp8) {
-    const float sa = p.a_scale[m];
+    const float sa = pre.sa;
     const float4 wl = *reinterpret_cast<const float4*>(p.w_scale + n_lo);
     const float4 wh = *reinterpret_cast<const float4*>(p.w_scale + n_hi);
     const float wlv[4] = {wl.x, wl.y, wl.z, wl.w}, whv[4] = {wh.x, wh.y, wh.z, wh.w};
@@ -104,7 +132,7 @@ DEVI void epilogue_rope(const GemmParams& p, int m, int n_lo, float4 lo, float4 
       h[e] = (h[e] * sa) * whv[e];
     }
   } else if (KIND == kKindNvfp4) {
-    const float sa = p.a_scale[m] * p.w_tensor_scale;
+    const float sa = pre.sa * p.w_tensor_scale;
 #pragma unroll
     for (int e = 0; e < 4; ++e) {
       l[e] *= sa;
@@ -122,11 +150,7 @@ DEVI void epilogue_rope(const GemmParams& p, int m, int n_lo, float4 lo, float4 
       h[e] += __bfloat162float(bha[e]);
     }
   }
-  const int pos = m % p.rope_seq, d0 = n_lo & 63;
-  const float4 c0 = *reinterpret_cast<const float4*>(p.rope_cos + (size_t)pos * 64 + d0);
-  const float4 c1 = *reinterpret_cast<const float4*>(p.rope_cos + (size_t)pos * 64 + d0 + 32);
-  const float4 s0 = *reinterpret_cast<const float4*>(p.rope_sin + (size_t)pos * 64 + d0);
-  const float4 s1 = *reinterpret_cast<const float4*>(p.rope_sin + (size_t)pos * 64 + d0 + 32);
+  const float4 c0 = pre.c0, c1 = pre.c1, s0 = pre.s0, s1 = pre.s1;
   const float cl[4] = {c0.x, c0.y, c0.z, c0.w}, ch[4] = {c1.x, c1.y, c1.z, c1.w};
   const float sl[4] = {s0.x, s0.y, s0.z, s0.w}, sh[4] = {s1.x, s1.y, s1.z, s1.w};
   __nv_bfloat16 ol[4], oh[4];
@@ -184,19 +208,22 @@ DEVI void tile_epilogue(const GemmParams& p, uint32_t tmem, float* part, int til
   else
     __syncthreads();
 
-  // ---- reduction over the cluster and the epilogue: a thread takes 4
-  // consecutive rows of one token and their partners (+64: the GEGLU gate;
-  // +32 in the rotary tiles of q and k: the rotation partner) and sums the S
-  // partials in rank order with 16-byte loads issued back to back.
+  // ---- reduction over the cluster and the epilogue: a thread (of all the
+  // CTA's threads) takes 4 consecutive rows of one token and their partners
+  // (+64: the GEGLU gate; +32 in the rotary tiles of q and k: the rotation
+  // partner) and sums the S partials in rank order with 16-byte loads issued
+  // back to back, together with the item's other global operands.
   const uint32_t part_addr = smem_u32(part);
   const bool rope = tile_n * 128 < p.rope_cols;
   const int pair = rope ? 32 : 64;
-  for (int item = tid; tid < 128 && item < nt * 16; item += 128) {
+  const bool residual = LNST || p.epilogue == kEpiResidual;
+  for (int item = tid; item < nt * 16; item += blockDim.x) {
     const int tl = t0 + (item >> 4);
     const int q4 = rope ? ((item >> 3) & 1) * 64 + (item & 7) * 4 : (item & 15) * 4;
     const int m = tile_m * BN + tl;
     if (m >= p.M) continue;
     const int off = tl * 128 + q4;
+    const EpiPre pre = epi_prefetch<KIND>(p, m, tile_n * 128 + q4, residual, rope);
     float4 lo, hi;
     if (split == 1) {
       lo = *reinterpret_cast<const float4*>(part + off);
@@ -233,7 +260,7 @@ DEVI void tile_epilogue(const GemmParams& p, uint32_t tmem, float* part, int til
       // are 16 consecutive threads (a 16-lane half warp)
       float4* rl = reinterpret_cast<float4*>(p.resid + (size_t)m * p.ldr + tile_n * 128 + q4);
       float4* rh = rl + 16;
-      float4 a = *rl, b = *rh;
+      float4 a = pre.ra, b = pre.rb;
       a.x += bf16_round(lo.x); a.y += bf16_round(lo.y); a.z += bf16_round(lo.z); a.w += bf16_round(lo.w);
       b.x += bf16_round(hi.x); b.y += bf16_round(hi.y); b.z += bf16_round(hi.z); b.w += bf16_round(hi.w);
       *rl = a;
@@ -255,9 +282,9 @@ DEVI void tile_epilogue(const GemmParams& p, uint32_t tmem, float* part, int til
       continue;
     }
     if (rope)
-      epilogue_rope<KIND>(p, m, tile_n * 128 + q4, lo, hi);
+      epilogue_rope<KIND>(p, m, tile_n * 128 + q4, lo, hi, pre);
     else
-      epilogue_quad<KIND>(p, m, tile_n * 128 + q4, tile_n * 64 + q4, lo, hi);
+      epilogue_quad<KIND>(p, m, tile_n * 128 + q4, tile_n * 64 + q4, lo, hi, pre);
   }
   if (split > 1 && !gpath) cluster_sync_all();
 
@@ -355,7 +382,7 @@ DEVI void tile_epilogue_wide(const GemmParams& p, const CUtensorMap* omap, uint3
   // THREADS is a multiple of `quads`, so every item of a thread covers the
   // same 4 rows: the per-row constants (weight scales, bias, the rotation
   // partner) are loaded once, and the rotary tables of a thread's tokens are
-  // loaded in batches of KB tokens ahead of the arithmetic (a load per item
+  // loaded KB tokens at a time ahead of the arithmetic (a load per item
   // left the loop latency-bound).
   static_assert(THREADS % 32 == 0, "wide epilogue: whole warps");
   const int q = tid % quads, r0 = 4 * q, n = tile_n * 128 + r0;
@@ -383,7 +410,7 @@ DEVI void tile_epilogue_wide(const GemmParams& p, const CUtensorMap* omap, uint3
 #pragma unroll
     for (int e = 0; e < 4; ++e) bx[e] = __bfloat162float(bb[e]);
   }
-  constexpr int KB = 4;
+  constexpr int KB = 4;  // 8 measured no faster (and spills with fp8's weight scales)
   for (int tb = tid / quads; tb < BN; tb += KB * tok_step) {
     float4 cv[KB], sv[KB];
     if (rot) {
