@@ -158,10 +158,11 @@ __global__ void __launch_bounds__(BN >= 128 ? 256 : 128, BN == 128 ? 2 : 1)
     atomicExch(failed, 1u);
   }
   tc_fence_after();
-  if (split == 1 && p.tma_epilogue && BN >= 128)
-    tile_epilogue_wide<BN, KIND, 256>(p, &omap, tmem, smem, tile_n, tile_m);
-  else
-    tile_epilogue<BN, KIND, LNST>(p, tmem, reinterpret_cast<float*>(smem), tile_n, tile_m, split, rank);
+  const bool wide = split == 1 && p.tma_epilogue && BN >= 128;
+  if constexpr (BN >= 128) {
+    if (wide) tile_epilogue_wide<BN, KIND, 256>(p, &omap, tmem, smem, tile_n, tile_m);
+  }
+  if (!wide) tile_epilogue<BN, KIND, LNST>(p, tmem, reinterpret_cast<float*>(smem), tile_n, tile_m, split, rank);
 
   // ---- teardown: drain copies still in flight after a failure, free TMEM
   if (tid == 0 && *failed) {

@@ -184,8 +184,23 @@ DEVI void tile_epilogue(const GemmParams& p, uint32_t tmem, float* part, int til
   if (gpath) part = p.partials + ((size_t)(tile_m * gridDim.x + tile_n) * split + rank) * BN * 128;
   // CTA `rank` owns the tokens [t0, t1) of the tile in the reduction below.
   const int t0 = rank * BN / split, t1 = (rank + 1) * BN / split, nt = t1 - t0;
-  if (tid >= 128) {
-    // CTAs of more than 128 threads: only warps 0-3 own TMEM lanes
+  if (BN >= 64 && blockDim.x >= 256) {
+    // two warps per TMEM lane quarter (warp w reads lanes 32*(w%4)..), each
+    // dumping half of the token columns
+    if (warp < 8) {
+      const int lq = warp & 3, c0 = (warp >> 2) * (BN / 2);
+      const uint32_t qaddr = tmem + ((uint32_t)(lq * 32) << 16);
+#pragma unroll 1
+      for (int c = c0; c < c0 + BN / 2; c += 32) {
+        uint32_t r[32];
+        tmem_ld32(qaddr + c, r);
+        tmem_wait_ld();
+#pragma unroll
+        for (int j = 0; j < 32; ++j) part[(c + j) * 128 + lq * 32 + (tid & 31)] = __uint_as_float(r[j]);
+      }
+    }
+  } else if (tid >= 128) {
+    // only warps 0-3 own TMEM lanes
   } else if (BN >= 32) {
 #pragma unroll 1
     for (int c = 0; c < BN; c += 32) {
@@ -308,23 +323,19 @@ DEVI void tile_epilogue_wide(const GemmParams& p, const CUtensorMap* omap, uint3
   float* P = reinterpret_cast<float*>(smem);
   __nv_bfloat16* O = reinterpret_cast<__nv_bfloat16*>(smem + BN * 512);
   float* S = reinterpret_cast<float*>(smem + BN * 512 + BN * 256);
-  if (tid < 128) {
-    const uint32_t lane_addr = tmem + ((uint32_t)(warp * 32) << 16);
-    constexpr int CH = BN >= 32 ? 32 : 16;
+  static_assert(THREADS == 256 && BN >= 64, "wide epilogue: two warpgroups, 64+ token columns");
+  {
+    // two warps per TMEM lane quarter (warp w reads lanes 32*(w%4)..), each
+    // dumping half of the token columns
+    const int lq = warp & 3, c0 = (warp >> 2) * (BN / 2);
+    const uint32_t lane_addr = tmem + ((uint32_t)(lq * 32) << 16);
 #pragma unroll 1
-    for (int c = 0; c < BN; c += CH) {
+    for (int c = c0; c < c0 + BN / 2; c += 32) {
       uint32_t v[32];
-      if (CH == 32) {
-        tmem_ld32(lane_addr + c, v);
-      } else {
-        uint32_t v16[16];
-        tmem_ld16(lane_addr + c, v16);
-#pragma unroll
-        for (int j = 0; j < 16; ++j) v[j] = v16[j];
-      }
+      tmem_ld32(lane_addr + c, v);
       tmem_wait_ld();
 #pragma unroll
-      for (int j = 0; j < CH; ++j) P[(c + j) * 128 + tid] = __uint_as_float(v[j]);
+      for (int j = 0; j < 32; ++j) P[(c + j) * 128 + lq * 32 + (tid & 31)] = __uint_as_float(v[j]);
     }
   }
   if (KIND != kKindBf16)
@@ -379,6 +390,65 @@ DEVI void tile_epilogue_wide(const GemmParams& p, const CUtensorMap* omap, uint3
     __syncthreads();
     return;
   }
+  if (tile_n * 128 + 128 <= p.rope_cols) {
+    // rotary tile (two q or k heads): a thread takes rows r0..r0+3 (d0 < 32),
+    // their partners r0+32.., and the same two row groups of the second head
+    // (+64), for tokens tid/8, +32, ...: one cos / sin pair (d0 and d0+32)
+    // serves all four, and a thread's four tokens are loaded in one batch.
+    const int r0 = 4 * (tid & 7);
+    float ws[4][4];
+#pragma unroll
+    for (int gq = 0; gq < 4; ++gq) {
+      ws[gq][0] = ws[gq][1] = ws[gq][2] = ws[gq][3] = 1.f;
+      if (KIND == kKindFp8) {
+        const float4 a = *reinterpret_cast<const float4*>(p.w_scale + tile_n * 128 + r0 + 32 * gq);
+        ws[gq][0] = a.x; ws[gq][1] = a.y; ws[gq][2] = a.z; ws[gq][3] = a.w;
+      }
+    }
+    constexpr int RT = BN / (THREADS / 8);  // tokens per thread
+    float4 c0[RT], c1[RT], s0[RT], s1[RT];
+#pragma unroll
+    for (int u = 0; u < RT; ++u) {
+      const int pos = (m_base + (tid >> 3) + u * (THREADS / 8)) % p.rope_seq;
+      c0[u] = *reinterpret_cast<const float4*>(p.rope_cos + (size_t)pos * 64 + r0);
+      c1[u] = *reinterpret_cast<const float4*>(p.rope_cos + (size_t)pos * 64 + r0 + 32);
+      s0[u] = *reinterpret_cast<const float4*>(p.rope_sin + (size_t)pos * 64 + r0);
+      s1[u] = *reinterpret_cast<const float4*>(p.rope_sin + (size_t)pos * 64 + r0 + 32);
+    }
+#pragma unroll
+    for (int u = 0; u < RT; ++u) {
+      const int tok = (tid >> 3) + u * (THREADS / 8);
+      const float cl[4] = {c0[u].x, c0[u].y, c0[u].z, c0[u].w}, ch[4] = {c1[u].x, c1[u].y, c1[u].z, c1[u].w};
+      const float sl[4] = {s0[u].x, s0[u].y, s0[u].z, s0[u].w}, sh[4] = {s1[u].x, s1[u].y, s1[u].z, s1[u].w};
+      const float sc = KIND == kKindNvfp4 ? S[tok] * tsc : KIND == kKindFp8 ? S[tok] : 1.f;
+#pragma unroll
+      for (int hd = 0; hd < 2; ++hd) {
+        const float4 la = *reinterpret_cast<const float4*>(P + tok * 128 + 64 * hd + r0);
+        const float4 ha = *reinterpret_cast<const float4*>(P + tok * 128 + 64 * hd + r0 + 32);
+        float l[4] = {la.x, la.y, la.z, la.w}, h[4] = {ha.x, ha.y, ha.z, ha.w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          if (KIND == kKindFp8) {
+            l[e] = (l[e] * sc) * ws[2 * hd][e];
+            h[e] = (h[e] * sc) * ws[2 * hd + 1][e];
+          } else if (KIND == kKindNvfp4) {
+            l[e] *= sc;
+            h[e] *= sc;
+          }
+        }
+        // bf16(qkv) rotated in fp32 without FMA, as rope_qkv does (kernels.py:62-93)
+        __nv_bfloat16 ol[4], oh[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float a = bf16_round(l[e]), b = bf16_round(h[e]);
+          ol[e] = __float2bfloat16_rn(__fadd_rn(__fmul_rn(a, cl[e]), __fmul_rn(-b, sl[e])));
+          oh[e] = __float2bfloat16_rn(__fadd_rn(__fmul_rn(b, ch[e]), __fmul_rn(a, sh[e])));
+        }
+        *reinterpret_cast<uint2*>(O + tok * 128 + 64 * hd + r0) = *reinterpret_cast<uint2*>(ol);
+        *reinterpret_cast<uint2*>(O + tok * 128 + 64 * hd + r0 + 32) = *reinterpret_cast<uint2*>(oh);
+      }
+    }
+  } else {
   // THREADS is a multiple of `quads`, so every item of a thread covers the
   // same 4 rows: the per-row constants (weight scales, bias, the rotation
   // partner) are loaded once, and the rotary tables of a thread's tokens are
@@ -486,6 +556,7 @@ DEVI void tile_epilogue_wide(const GemmParams& p, const CUtensorMap* omap, uint3
         *reinterpret_cast<uint2*>(O + tok * 128 + r0) = *reinterpret_cast<uint2*>(o);
       }
     }
+  }
   }
   fence_proxy_async_smem();
   __syncthreads();
