@@ -257,6 +257,10 @@ void gemm_plan(int M, int N, int kblocks, int sm_count, int* bn_out, int* split_
   // token tiles of <= 64 fit two CTAs per SM: split until about two per SM
   // (measured 937 -> 933 us per batch-1 forward)
   *split_out = gemm_split(tiles, kblocks, bn <= 64 ? 2 * sm_count : sm_count, 8);
+  // 128-token tiles that leave SMs idle and run a long K loop (Wo2 at 1.5k
+  // tokens: 96 tiles x 21 K blocks) split K in two: C2 2.58 -> 2.51 ms (the
+  // same for Wo's 8 K blocks measured slower, 2.55 ms)
+  if (bn == 128 && *split_out == 1 && tiles < sm_count && kblocks >= 16) *split_out = 2;
 }
 
 int gemm_token_tile(int M) {
