@@ -316,12 +316,14 @@ def run_batched(args):
 
     # device time per step: the step's graphs replayed back to back with inputs resident
     dev_ms = []
+    launches = 0  # kernels launched by the timed replays
     for plan in plans:
         t = 0.0
         for req in plan:
             eng._run_on(req, eng)                 # lane 0: its staging buffer now holds req
             slot = eng.graphs[eng._graph_key(req)]
             t += float(np.mean(eng.native.replay_device(slot, 5)))
+            launches += 5 * eng.native.kernel_count(slot)
         dev_ms.append(t)
     with ClockSampler(local) as clocks:
         barrier()
@@ -372,6 +374,7 @@ def run_batched(args):
                              "peak_source": f"{'2x' if precision == 'fp8' else '4x' if precision == 'nvfp4' else '1x'} "
                                             "measured cuBLAS bf16 (MEASURED_PEAKS.json)"},
                 **({"serving_lanes": lanes_line} if lanes_line else {}),
+                "gpu_launches": launches,
                 "clocks": cs}
         print(json.dumps(line), flush=True)
     eng.close()
