@@ -167,9 +167,11 @@ DEVI void epilogue_rope(const GemmParams& p, int m, int n_lo, float4 lo, float4 
 
 // TMEM accumulator -> partial (L2 scratch p.partials, or the shared scratch
 // `part`) -> cluster reduction -> epilogue.  Called by all threads of the CTA
-// after the MMA-done barrier completed (threads 0-127 hold the TMEM lanes and
-// do the work).  `part` is at least BN*128 floats of shared memory (the
-// pipeline region, free once every MMA has completed).
+// after the MMA-done barrier completed: warps 0-3 read the TMEM lane quarters
+// (in 256-thread CTAs warps 4-7 read the same quarters' upper token columns),
+// and every thread takes part in the reduction.  `part` is at least BN*128
+// floats of shared memory (the pipeline region, free once every MMA has
+// completed).
 // LNST: residual epilogue that also writes the LayerNorm statistics of the
 // updated rows (p.ln_stats; bf16 projections without bias).
 template <int BN, int KIND, bool LNST = false>
@@ -305,10 +307,11 @@ DEVI void tile_epilogue(const GemmParams& p, uint32_t tmem, float* part, int til
 
 }
 
-// Epilogue of an unsplit tile with THREADS (256) threads.  Warps 0-3 (the
-// four TMEM lane quarters) dump the raw fp32 accumulator into shared memory
+// Epilogue of an unsplit tile with THREADS (256) threads.  The eight warps,
+// two per TMEM lane quarter, dump the raw fp32 accumulator into shared memory
 // as P[token][128 weight rows]; then every thread takes (token, 4 rows)
-// items, applies the precision's scales, bias and activation, and either
+// items (rotary tiles: a token's rows r, r+32, r+64, r+96 that share one
+// cos / sin pair), applies the precision's scales, bias and activation, and either
 // writes the bf16 result into a shared [token][features] tile that one TMA
 // store copies out (store / ReLU / GELU / GEGLU), or updates the fp32
 // residual in global memory with 16-byte loads issued eight items at a time.
