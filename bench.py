@@ -186,8 +186,9 @@ class ClockSampler:
         return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
 
 
-def cpu_baseline(cfg, seconds, precision="bf16", max_steps=None):
-    """Time the CPU oracle port of the reference forward on this host."""
+def cpu_baseline(cfg, seconds, precision="bf16", max_steps=None, warmup=1):
+    """Time the CPU oracle port of the reference forward on this host
+    (`warmup` untimed forwards first, bounded to a quarter of `seconds`)."""
     import torch
     from laya_b200.weights import seeded_weights
     from oracle.laya_oracle import Oracle
@@ -196,7 +197,10 @@ def cpu_baseline(cfg, seconds, precision="bf16", max_steps=None):
     orc = Oracle(w, cfg, precision)
     del w
     _, inp = workload(cfg)
-    orc.forward(**inp)  # warm-up
+    warm, t_warm = 0, time.perf_counter() + seconds / 4
+    while warm < max(1, warmup) and (warm == 0 or time.perf_counter() < t_warm):
+        orc.forward(**inp)
+        warm += 1
     times = []
     t_end = time.perf_counter() + seconds
     while time.perf_counter() < t_end and (max_steps is None or len(times) < max_steps):
@@ -207,7 +211,7 @@ def cpu_baseline(cfg, seconds, precision="bf16", max_steps=None):
     return {"value": len(times) / total, "unit": UNIT, "cores": torch.get_num_threads(), "kind": "port",
             "sample": f"{len(times)} forwards of b=1 s=64 noul (one decision each), {total:.1f} s, "
                       f"oracle/laya_oracle.py fp32-with-bf16-rounding restatement on {os.cpu_count()} host cores",
-            "ms_per_forward": 1000 * total / len(times), "steps": len(times)}
+            "ms_per_forward": 1000 * total / len(times), "steps": len(times), "warmup": warm}
 
 
 def dist_setup(n):
@@ -230,10 +234,10 @@ def run_reference(args):
             return 0
     from laya_b200.config import LAYA
     budget = max(10.0, min(120.0, args.cpu_seconds * 4))
-    base = cpu_baseline(LAYA, budget, max_steps=args.steps)
+    base = cpu_baseline(LAYA, budget, max_steps=args.steps, warmup=args.warmup)
     steps = base["steps"]
     line = {"metric": METRIC, "value": base["value"], "unit": UNIT, "n_gpus": args.gpus, "steps": steps,
-            "requested_steps": args.steps, "warmup": 1, "ms_per_step": base["ms_per_forward"],
+            "requested_steps": args.steps, "warmup": base["warmup"], "ms_per_step": base["ms_per_forward"],
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic", "impl": "reference",
             "config": {"workload": "C1: b=1, s=64, one noul question (k=2), bf16 weights",
