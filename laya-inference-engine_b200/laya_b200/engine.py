@@ -222,8 +222,13 @@ class B200Engine:
     # -- shapes (engine.py:112-138)
     def _shape(self, prepared):
         count = len(prepared.items)
-        length = max(len(x["ids"]) for x in prepared.items)
-        options = max(2, max(len(x["markers"]) for x in prepared.items))
+        length, options = 0, 2
+        for x in prepared.items:
+            n, k = len(x["ids"]), len(x["markers"])
+            if n > length:
+                length = n
+            if k > options:
+                options = k
         max_len = self.cfg.get("max_len", 512)
         length = next((x for x in self.sequence_buckets if length <= x <= max_len), max_len)
         batch = min(self.max_questions, 1 << (count - 1).bit_length())
@@ -251,24 +256,30 @@ class B200Engine:
         bufs = io.get(key)
         if bufs is None:
             batch, length, options = key[:3]
-            arrays = {"input_ids": np.empty((batch, length), np.int64),
-                      "attention_mask": np.empty((batch, length), np.int64),
-                      "marker_pos": np.empty((batch, options), np.int64),
+            # the int64 inputs are views of one block, reset from a pristine
+            # copy (pad ids, dummy rows seeing their position 0) in one copy
+            cuts = np.cumsum([batch * length, batch * length, batch * options, batch])
+            ints = np.empty(int(cuts[-1]), np.int64)
+            ids, mask, mpos, qtype = np.split(ints, cuts[:-1])
+            arrays = {"input_ids": ids.reshape(batch, length),
+                      "attention_mask": mask.reshape(batch, length),
+                      "marker_pos": mpos.reshape(batch, options),
                       "marker_mask": np.empty((batch, options), np.uint8),
-                      "qtype": np.empty(batch, np.int64),
+                      "qtype": qtype,
                       "logits": np.empty((batch, options), np.float32),
                       "act": np.empty((batch, 2), np.float32)}
-            bufs = io[key] = (arrays, tuple(a.ctypes.data for a in arrays.values()))
-        arrays, addresses = bufs
+            clean_ints = np.zeros_like(ints)
+            clean_ints[:batch * length] = self.pad_token_id
+            clean_ints[batch * length:2 * batch * length].reshape(batch, length)[:, 0] = 1
+            clean_mmask = np.zeros((batch, options), np.uint8)
+            clean_mmask[:, 0] = 1
+            bufs = io[key] = (arrays, tuple(a.ctypes.data for a in arrays.values()), ints, clean_ints,
+                              clean_mmask)
+        arrays, addresses, ints, clean_ints, clean_mmask = bufs
         ids, mask, mpos, mmask, qtype = (arrays[n] for n in ("input_ids", "attention_mask", "marker_pos",
                                                              "marker_mask", "qtype"))
-        ids.fill(self.pad_token_id)
-        mask.fill(0)
-        mpos.fill(0)
-        mmask.fill(0)
-        qtype.fill(0)
-        mask[:, 0] = 1
-        mmask[:, 0] = 1
+        np.copyto(ints, clean_ints)
+        np.copyto(mmask, clean_mmask)
         for i, item in enumerate(prepared.items):
             n, k = len(item["ids"]), len(item["markers"])
             ids[i, :n] = item["ids"]
