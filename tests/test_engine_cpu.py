@@ -188,7 +188,10 @@ def test_run_packs_into_kept_host_arrays_like_fill():
     engine.native = AddressNative()
     first = synthetic_items([64, 40, 12], ["choice", "noul", "score"], seed=4, vocab=1000)
     second = synthetic_items([30, 20], ["noul", "noul"], seed=5, vocab=1000)
-    for items in (first, second, first):
+    # same graph key as `first`, other row lengths and options: every stale
+    # value of the previous call must be reset
+    third = synthetic_items([12, 64, 7], ["score", "choice", "noul"], seed=6, vocab=1000)
+    for items in (first, second, first, third):
         prepared = request_from_items(items)
         engine.run_prepared(prepared)
         shape = engine._shape(prepared)
