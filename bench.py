@@ -19,7 +19,8 @@ barriers and the max-over-ranks of the timed region.
 * roofline: the projection GEMM family (the dominant kernel), timed live as a
   graph of the forward's GEMM launches only; algorithmic bytes = weight bytes
   + activation bytes each launch must move.
-* cpu_baseline: the CPU oracle port of the reference forward, timed on this
+* cpu_baseline: the CPU oracle port of the reference forward (its bf16 Linears
+  through torch's bf16 GEMM, the reference's own CPU arithmetic), timed on this
   host's cores on a bounded sample of the same request.
 """
 import argparse
@@ -194,7 +195,7 @@ def cpu_baseline(cfg, seconds, precision="bf16", max_steps=None, warmup=1):
     from oracle.laya_oracle import Oracle
     torch.set_num_threads(os.cpu_count() or 1)
     w = seeded_weights(cfg, seed=0)
-    orc = Oracle(w, cfg, precision)
+    orc = Oracle(w, cfg, precision, bf16_gemm=True)  # bf16 Linears as the reference runs them on a CPU
     del w
     _, inp = workload(cfg)
     warm, t_warm = 0, time.perf_counter() + seconds / 4
@@ -210,7 +211,8 @@ def cpu_baseline(cfg, seconds, precision="bf16", max_steps=None, warmup=1):
     total = sum(times)
     return {"value": len(times) / total, "unit": UNIT, "cores": torch.get_num_threads(), "kind": "port",
             "sample": f"{len(times)} forwards of b=1 s=64 noul (one decision each), {total:.1f} s, "
-                      f"oracle/laya_oracle.py fp32-with-bf16-rounding restatement on {os.cpu_count()} host cores",
+                      f"oracle/laya_oracle.py port, bf16 Linears through torch's bf16 GEMM as the reference's "
+                      f"nn.Linear runs on a CPU, on {os.cpu_count()} host cores",
             "ms_per_forward": 1000 * total / len(times), "steps": len(times), "warmup": warm}
 
 

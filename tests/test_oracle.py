@@ -16,10 +16,10 @@ CONFIGS = {"laya": LAYA, "tiny": TINY}
 
 
 @functools.lru_cache(maxsize=2)
-def oracle_for(name, precision="bf16"):
+def oracle_for(name, precision="bf16", bf16_gemm=False):
     cfg = CONFIGS[name]
     w = seeded_weights(cfg, seed=0)
-    return O.Oracle(w, cfg, precision), weights_digest(w)
+    return O.Oracle(w, cfg, precision, bf16_gemm=bf16_gemm), weights_digest(w)
 
 
 def load_golden(path):
@@ -28,10 +28,14 @@ def load_golden(path):
     return z, {k: z[k] for k in keys}
 
 
+@pytest.mark.parametrize("bf16_gemm", [False, True], ids=["fp32-restatement", "bf16-gemm"])
 @pytest.mark.parametrize("path", sorted(GOLDEN.glob("*.npz")), ids=lambda p: p.stem)
-def test_oracle_matches_reference_forward(path):
+def test_oracle_matches_reference_forward(path, bf16_gemm):
+    """Both oracle modes: the fp32-accumulating restatement the parity tests
+    use, and the bf16-GEMM mode (the reference's CPU arithmetic) that the
+    benchmark's CPU reference arm times."""
     z, inputs = load_golden(path)
-    oracle, digest = oracle_for(str(z["config"]))
+    oracle, digest = oracle_for(str(z["config"]), "bf16", bf16_gemm)
     assert str(z["weights_sha256"]) == digest, "seeded weight generator drifted"
     logits, act = oracle.forward(**inputs)
     n = int(z["n_items"])
