@@ -126,8 +126,9 @@ typedef struct laya_b200_tail_args {
   int32_t options;           /* padded option count k, 2..256 */
   int32_t hidden;            /* d */
   int32_t act_hidden;        /* act_head width; questions * act_hidden <= 65536 */
-  const void* z;             /* bf16 [questions*options][hidden]: gelu(scorer.fc1) of the option rows */
-  const void* fc2_w;         /* bf16 [hidden]: scorer.fc2 weight */
+  const void* z;             /* bf16 [questions*options][hidden]: gelu(scorer.fc1) of the option rows;
+                                16-byte aligned */
+  const void* fc2_w;         /* bf16 [hidden]: scorer.fc2 weight; 16-byte aligned */
   const void* fc2_b;         /* bf16 [1] */
   const int32_t* marker_mask;/* int32 [questions][options], nonzero = real option */
   const float* h_sel;        /* fp32 [questions*(1+options)][hidden]: CLS row then option rows */

@@ -1387,6 +1387,9 @@ int laya_b200_run(laya_b200_engine* e, int slot, const int64_t* input_ids, const
         w[L.score + q * k + j] = q * (1 + k) + 1 + j;
       }
     }
+    // The copy below overwrites the staging buffer with this slot's layout:
+    // until it has completed, no slot's inputs are known to be resident.
+    e->inputs_slot = -1;
     if (e->sync_check) {
       ck(cudaMemcpyAsync(e->d_in, e->h_in, L.words * 4, cudaMemcpyHostToDevice, e->stream), "H2D");
       e->launches = 0;

@@ -75,6 +75,11 @@ extern "C" int laya_b200_tail_noalloc(const laya_b200_tail_args* a, void* stream
   if (!a->z || !a->fc2_w || !a->fc2_b || !a->marker_mask || !a->h_sel || !a->a1_w || !a->a1_b || !a->a2_w ||
       !a->a2_b || !a->logits || !a->act)
     return reject("null buffer");
+  // z and fc2_w are read 16 bytes at a time by the kernel: a pointer from a
+  // caller's pool that is only 8-byte aligned would fault on the GPU, so it is
+  // refused here instead.
+  if ((reinterpret_cast<uintptr_t>(a->z) | reinterpret_cast<uintptr_t>(a->fc2_w)) & 15)
+    return reject("z and fc2_w must be 16-byte aligned device pointers");
   int device = 0;
   cudaError_t err = cudaGetDevice(&device);
   if (err != cudaSuccess) return reject(std::string("cudaGetDevice: ") + cudaGetErrorString(err));

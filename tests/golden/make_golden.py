@@ -1,9 +1,11 @@
 """Generate the golden fixtures by running the reference's own forward on CPU.
 
-Run in a container that has the reference sources (``LAYA_REFERENCE_SRC``,
-default ``/root/reference/src``) and ``transformers``:
+Run where the reference sources and ``transformers`` are importable, naming
+the reference's ``src`` directory (the one holding ``laya_blackwell``):
 
-    python tests/golden/make_golden.py
+    python tests/golden/make_golden.py <reference-src-dir>
+
+(or set ``LAYA_REFERENCE_SRC`` to it).
 
 What it does, per case:
 1. builds a Laya-shaped network from ``transformers.ModernBertModel`` and torch
@@ -123,7 +125,9 @@ CASES = [
 
 
 def main():
-    ref_src = os.environ.get("LAYA_REFERENCE_SRC", "/root/reference/src")
+    ref_src = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("LAYA_REFERENCE_SRC")
+    if not ref_src:
+        raise SystemExit("usage: make_golden.py <reference-src-dir> (or set LAYA_REFERENCE_SRC)")
     sys.path.insert(0, ref_src)
     import transformers
     import laya_blackwell.model as ref_model

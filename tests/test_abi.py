@@ -57,3 +57,17 @@ def test_tail_noalloc_validates_before_any_cuda_call():
     args = _lib.TailArgs(questions=0, options=4, hidden=256, act_hidden=64)
     assert lib.laya_b200_tail_noalloc(ctypes.byref(args), None) != 0
     assert b"questions" in lib.laya_b200_last_error(None)
+
+
+def test_tail_noalloc_rejects_unaligned_vector_operands():
+    """z and fc2_w are read 16 bytes at a time on the GPU; a pointer that is
+    only 8-byte aligned is refused on the host before any CUDA call."""
+    lib = _lib.load()
+    base = 1 << 20
+    good = dict(questions=2, options=4, hidden=256, act_hidden=64, fc2_b=base, marker_mask=base, h_sel=base,
+                a1_w=base, a1_b=base, a2_w=base, a2_b=base, logits=base, act=base)
+    for name in ("z", "fc2_w"):
+        ptrs = {"z": base, "fc2_w": base, name: base + 8}
+        args = _lib.TailArgs(**good, **ptrs)
+        assert lib.laya_b200_tail_noalloc(ctypes.byref(args), None) != 0
+        assert b"16-byte aligned" in lib.laya_b200_last_error(None)
