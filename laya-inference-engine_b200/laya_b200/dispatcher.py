@@ -14,11 +14,16 @@ independent questions are partitioned across GPUs:
   forward (batch padded to a power of two, as ``BlackwellEngine._shape``).
 
 There is no collective anywhere: results return to the caller's thread.
-Failure handling is on the host: a worker that raises or exceeds ``timeout``
-marks its GPU unhealthy, and its questions are re-run on the healthy GPUs
-(``retry=True``) or reported as errors.
+Failure handling is on the host: a worker that raises, or that has not
+finished when the round's single deadline (``timeout`` seconds after the round
+was dispatched) passes, marks its GPU unhealthy, and its questions are re-run
+on the healthy GPUs (``retry=True``) or reported as errors.  ``readmit()``
+probes unhealthy GPUs whose worker has returned and puts them back in service
+when a probe request succeeds.  ``close()`` never waits on a worker that is
+still stuck: its pool is shut down without waiting and its engine is left open
+(closing it under a running native call would free memory the call uses).
 """
-from concurrent.futures import ThreadPoolExecutor, TimeoutError as FutureTimeout
+from concurrent.futures import ThreadPoolExecutor, wait as futures_wait
 import threading
 
 import numpy as np
@@ -90,6 +95,7 @@ class B200Dispatcher:
         self.pools = {d: ThreadPoolExecutor(max_workers=1, thread_name_prefix=f"laya-gpu{d}")
                       for d in self.devices}
         self.healthy = {d: True for d in self.devices}
+        self.inflight = {d: None for d in self.devices}   # last future submitted to each worker
         self.lock = threading.Lock()
         self.closed = False
 
@@ -125,30 +131,66 @@ class B200Dispatcher:
             for d, shard in zip(alive, shards):
                 idx = [pending[j] for j in shard]
                 if idx:
-                    futs[d] = (idx, self.pools[d].submit(self._run_batches, d, items,
-                                                         group_by_bucket(items, idx, self.buckets, self.max_batch)))
+                    fut = self.pools[d].submit(self._run_batches, d, items,
+                                               group_by_bucket(items, idx, self.buckets, self.max_batch))
+                    self.inflight[d] = fut
+                    futs[d] = (idx, fut)
+            # one deadline for the whole round, however many GPUs take part
+            futures_wait([f for _, f in futs.values()], timeout=self.timeout)
             failed = []
             for d, (idx, fut) in futs.items():
-                try:
-                    results.update(fut.result(timeout=self.timeout))
-                except (Exception, FutureTimeout) as exc:  # noqa: BLE001 - any worker failure
-                    with self.lock:
-                        self.healthy[d] = False
-                    errors[d] = repr(exc)
-                    failed.extend(idx)
+                exc = None
+                if not fut.done():
+                    exc = TimeoutError(f"gpu {d} did not finish within {self.timeout} s")
+                elif fut.exception() is not None:
+                    exc = fut.exception()
+                if exc is None:
+                    results.update(fut.result())
+                    continue
+                with self.lock:
+                    self.healthy[d] = False
+                errors[d] = repr(exc)
+                failed.extend(idx)
             if failed and not self.retry:
                 raise RuntimeError(f"GPU worker failures: {errors}")
             pending = sorted(failed)
         return [results[i] for i in range(len(items))]
 
+    def _idle(self, device):
+        fut = self.inflight[device]
+        return fut is None or fut.done()
+
+    def readmit(self, probe_items, timeout=None):
+        """Probe every unhealthy GPU whose worker has returned with
+        `probe_items` (a small request) and mark it healthy again when the probe
+        succeeds.  Returns the devices put back in service."""
+        if self.closed:
+            raise RuntimeError("Dispatcher is closed")
+        back = []
+        for d in self.devices:
+            with self.lock:
+                if self.healthy[d] or not self._idle(d):
+                    continue
+            batches = group_by_bucket(probe_items, list(range(len(probe_items))), self.buckets, self.max_batch)
+            fut = self.pools[d].submit(self._run_batches, d, probe_items, batches)
+            self.inflight[d] = fut
+            futures_wait([fut], timeout=timeout if timeout is not None else self.timeout)
+            if fut.done() and fut.exception() is None:
+                with self.lock:
+                    self.healthy[d] = True
+                back.append(d)
+        return back
+
     def close(self):
         if self.closed:
             return
         self.closed = True
-        for p in self.pools.values():
-            p.shutdown(wait=True)
-        for e in self.engines.values():
-            e.close()
+        for d in self.devices:
+            if self._idle(d):
+                self.pools[d].shutdown(wait=True)
+                self.engines[d].close()
+            else:  # a worker still inside a call: do not wait for it, do not free its engine
+                self.pools[d].shutdown(wait=False, cancel_futures=True)
 
     def __enter__(self):
         return self

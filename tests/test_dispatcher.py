@@ -93,6 +93,60 @@ def test_timeout_marks_gpu_unhealthy_and_errors_without_retry():
         assert d.healthy[1] is False
 
 
+def test_one_deadline_for_the_whole_round():
+    """Four slow GPUs each overrun the limit: the round still fails after about
+    one timeout, not one timeout per GPU."""
+    def factory(device, **_):
+        return FakeEngine(device, delay=0.6)
+
+    with B200Dispatcher(devices=[0, 1, 2, 3], engine_factory=factory, timeout=0.15, retry=False) as d:
+        t0 = time.perf_counter()
+        with pytest.raises(RuntimeError, match="worker failures"):
+            d.run_items(items_of([100, 200, 300, 400]))
+        assert time.perf_counter() - t0 < 0.45
+        assert not any(d.healthy.values())
+
+
+def test_close_does_not_wait_for_a_stuck_worker_and_keeps_its_engine():
+    engines = {}
+    release = threading.Event()
+
+    class Stuck(FakeEngine):
+        def run_prepared(self, prepared):
+            release.wait(5)
+            return super().run_prepared(prepared)
+
+    def factory(device, **_):
+        engines[device] = Stuck(device) if device == 1 else FakeEngine(device)
+        return engines[device]
+
+    d = B200Dispatcher(devices=[0, 1], engine_factory=factory, timeout=0.1)
+    out = d.run_items(items_of([100, 200, 300, 400]))
+    assert d.healthy == {0: True, 1: False} and all(int(a[0]) == 0 for _, a in out)
+    t0 = time.perf_counter()
+    d.close()
+    assert time.perf_counter() - t0 < 1.0
+    assert engines[0].closed and not engines[1].closed     # never freed under a running call
+    release.set()
+
+
+def test_readmit_puts_a_recovered_gpu_back_in_service():
+    engines = {}
+
+    def factory(device, **_):
+        engines[device] = FakeEngine(device, fail=(device == 1))
+        return engines[device]
+
+    with B200Dispatcher(devices=[0, 1], engine_factory=factory) as d:
+        d.run_items(items_of([100, 200]))
+        assert d.healthy[1] is False
+        assert d.readmit(items_of([40])) == []          # still failing: stays out
+        engines[1].fail = False
+        assert d.readmit(items_of([40])) == [1]
+        out = d.run_items(items_of([100, 200, 300, 400]))
+        assert {int(a[0]) for _, a in out} == {0, 1}
+
+
 def test_all_gpus_failing_raises():
     with B200Dispatcher(devices=[0, 1], engine_factory=lambda dev, **_: FakeEngine(dev, fail=True)) as d:
         with pytest.raises(RuntimeError, match="no healthy GPU"):
