@@ -19,9 +19,20 @@ barriers and the max-over-ranks of the timed region.
 * roofline: the projection GEMM family (the dominant kernel), timed live as a
   graph of the forward's GEMM launches only; algorithmic bytes = weight bytes
   + activation bytes each launch must move.
-* cpu_baseline: the CPU oracle port of the reference forward (its bf16 Linears
-  through torch's bf16 GEMM, the reference's own CPU arithmetic), timed on this
-  host's cores on a bounded sample of the same request.
+* cpu_baseline: the reference's own forward (FastDecisionModel from the
+  offline install in baseline/_ref, its Triton RoPE replaced by the torch
+  restatement the CPU needs) timed on this host's cores on a bounded sample of
+  the same request; when the reference cannot be imported, the CPU oracle port
+  (its bf16 Linears through torch's bf16 GEMM), labelled "port".
+* configs: the other BASELINE configs measured in the same run, bounded to a
+  few seconds each: C2 (FP8, 16 x 96), C3 (NVFP4, 1 x 512) and C4 (FP8, 64
+  questions of s ~ U[32, 512] bucketed by 32; under torchrun its questions are
+  sharded over the ranks by LPT: strong scaling), each with its device value,
+  end-to-end value and tensor roofline.
+* reference_gpu: the reference's own bf16 path on the same GPU (FastDecisionModel
+  with its Triton RoPE under a CUDA graph, as BlackwellEngine._slot captures
+  it), on the C1 request, C3's shape in bf16 and, with the reference's
+  FP8Linear encoder, C1 and C2 in FP8: the GPU figure to beat.
 """
 import argparse
 import json
@@ -56,6 +67,10 @@ def parse():
                     help="c1: start each forward from the token tables (515 MB per GPU)")
     ap.add_argument("--lanes", type=int, default=2,
                     help="c1 / c4: also time this many serving lanes working at once (1: skip)")
+    ap.add_argument("--no-configs", action="store_true", help="c1: skip the C2 / C3 / C4 legs")
+    ap.add_argument("--no-reference-gpu", action="store_true", help="c1: skip the reference-on-this-GPU leg")
+    ap.add_argument("--config-steps", type=int, default=20,
+                    help="c1: timed steps of each of the C2 / C3 / C4 legs (C4: a quarter of it, at least 4)")
     ap.add_argument("--workload", default="c1", choices=["c1", "c2", "c3", "c4"],
                     help="c1 (default, the contract line): b=1 s=64 noul; c2: FP8 16x96; c3: NVFP4 1x512; "
                          "c4: FP8 64 questions s~U[32,512] bucketed by 32, sharded over ranks")
@@ -187,32 +202,60 @@ class ClockSampler:
         return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
 
 
-def cpu_baseline(cfg, seconds, precision="bf16", max_steps=None, warmup=1):
-    """Time the CPU oracle port of the reference forward on this host
-    (`warmup` untimed forwards first, bounded to a quarter of `seconds`)."""
+def _reference_cpu_model(cfg, weights):
+    """The reference's FastDecisionModel on the CPU (RoPE shim), or None with
+    the reason when the reference package cannot be imported."""
+    try:
+        from baseline import laya_net
+        return laya_net.build(cfg, weights, "cpu", rope="shim"), None
+    except Exception as exc:  # noqa: BLE001 - any import / build failure falls back to the port
+        return None, f"{type(exc).__name__}: {exc}"
+
+
+def cpu_baseline(cfg, seconds, precision="bf16", max_steps=None, warmup=1, weights=None):
+    """Time the reference's own CPU forward on this host (`warmup` untimed
+    forwards first, bounded to a quarter of `seconds`); the oracle port when
+    the reference cannot be imported."""
     import torch
     from laya_b200.weights import seeded_weights
-    from oracle.laya_oracle import Oracle
     torch.set_num_threads(os.cpu_count() or 1)
-    w = seeded_weights(cfg, seed=0)
-    orc = Oracle(w, cfg, precision, bf16_gemm=True)  # bf16 Linears as the reference runs them on a CPU
-    del w
+    w = weights if weights is not None else seeded_weights(cfg, seed=0)
     _, inp = workload(cfg)
+    model, why = _reference_cpu_model(cfg, w)
+    if model is not None:
+        from baseline import laya_net
+        kind = "reference"
+        tin = {k: torch.from_numpy(v) for k, v in inp.items()}
+        laya_net.use_rope("shim")
+
+        def fwd():
+            with torch.inference_mode():
+                model(**tin, global_attention_unmasked=True)
+        what = ("the reference's FastDecisionModel.forward (baseline/_ref, bf16 Linears, fp32 residuals; its "
+                "Triton RoPE replaced by the torch restatement of tests/test_kernels.py:42-49)")
+    else:
+        from oracle.laya_oracle import Oracle
+        kind = "port"
+        orc = Oracle(w, cfg, precision, bf16_gemm=True)  # bf16 Linears as the reference runs them on a CPU
+
+        def fwd():
+            orc.forward(**inp)
+        what = (f"oracle/laya_oracle.py port (reference not importable: {why}), bf16 Linears through torch's "
+                "bf16 GEMM as the reference's nn.Linear runs on a CPU")
     warm, t_warm = 0, time.perf_counter() + seconds / 4
     while warm < max(1, warmup) and (warm == 0 or time.perf_counter() < t_warm):
-        orc.forward(**inp)
+        fwd()
         warm += 1
     times = []
     t_end = time.perf_counter() + seconds
     while time.perf_counter() < t_end and (max_steps is None or len(times) < max_steps):
         t0 = time.perf_counter()
-        orc.forward(**inp)
+        fwd()
         times.append(time.perf_counter() - t0)
     total = sum(times)
-    return {"value": len(times) / total, "unit": UNIT, "cores": torch.get_num_threads(), "kind": "port",
-            "sample": f"{len(times)} forwards of b=1 s=64 noul (one decision each), {total:.1f} s, "
-                      f"oracle/laya_oracle.py port, bf16 Linears through torch's bf16 GEMM as the reference's "
-                      f"nn.Linear runs on a CPU, on {os.cpu_count()} host cores",
+    return {"value": len(times) / total, "unit": UNIT, "cores": torch.get_num_threads(), "kind": kind,
+            "sample": f"{len(times)} forwards of b=1 s=64 noul (one decision each), {total:.1f} s, {what}, "
+                      f"on {os.cpu_count()} host cores",
             "ms_per_forward": 1000 * total / len(times), "steps": len(times), "warmup": warm}
 
 
@@ -237,6 +280,9 @@ def run_reference(args):
     from laya_b200.config import LAYA
     budget = max(10.0, min(120.0, args.cpu_seconds * 4))
     base = cpu_baseline(LAYA, budget, max_steps=args.steps, warmup=args.warmup)
+    if base["kind"] != "reference":
+        print(f"reference arm: the reference could not be imported, timing the oracle port "
+              f"({base['sample']})", file=sys.stderr)
     steps = base["steps"]
     line = {"metric": METRIC, "value": base["value"], "unit": UNIT, "n_gpus": args.gpus, "steps": steps,
             "requested_steps": args.steps, "warmup": base["warmup"], "ms_per_step": base["ms_per_forward"],
@@ -273,121 +319,216 @@ def encoder_flops(cfg, items):
     return fl
 
 
-def run_batched(args):
-    """C2 / C3 / C4: batched requests through the public engine API."""
-    rank, world, local, dist = dist_setup(args.gpus)
-    import torch
-    from laya_b200.config import LAYA
-    from laya_b200.engine import B200Engine, request_from_items
+def batched_plan(w, cfg):
+    """(precision, sequence buckets, list of steps' items) of workload c2 / c3 / c4."""
     from laya_b200.workload import synthetic_items, mixed_kinds
-    from laya_b200.dispatcher import c4_step, shard_for_rank, group_by_bucket
-    cfg = LAYA
-    w = args.workload
+    from laya_b200.dispatcher import c4_step
     if w == "c2":
-        precision, buckets = "fp8", (96,)
-        steps_items = [synthetic_items([96] * 16, mixed_kinds(16, s), seed=100 + s, vocab=cfg.vocab) for s in range(2)]
-    elif w == "c3":
-        precision, buckets = "nvfp4", (512,)
-        steps_items = [synthetic_items([512], ["choice"], seed=200 + s, vocab=cfg.vocab) for s in range(2)]
-    else:
-        precision, buckets = "fp8", tuple(range(32, 513, 32))
-        steps_items = [c4_step(300 + s, cfg.vocab) for s in range(4)]
-    lanes = max(1, args.lanes) if w == "c4" else 1   # C4 steps hold several bucket groups
-    eng = B200Engine(config=cfg, device=local, precision=precision, max_questions=64, max_options=4,
-                     max_graphs=512, sequence_buckets=buckets, lanes=lanes)
-    plans = []
-    for items in steps_items:
-        mine = shard_for_rank(items, world, rank, buckets) if world > 1 else list(range(len(items)))
-        groups = group_by_bucket(items, mine, buckets, 64)
-        plans.append([request_from_items([items[i] for i in idx]) for _, idx in groups])
-    for plan in plans * max(1, args.warmup // len(plans)):     # captures every shape, then warm
-        for req in plan:
-            eng._run_on(req, eng)
-    for lane in eng._lanes[1:]:                  # every lane holds every shape's graph
-        for plan in plans:
+        return "fp8", (96,), [synthetic_items([96] * 16, mixed_kinds(16, s), seed=100 + s, vocab=cfg.vocab)
+                              for s in range(2)]
+    if w == "c3":
+        return "nvfp4", (512,), [synthetic_items([512], ["choice"], seed=200 + s, vocab=cfg.vocab) for s in range(2)]
+    return "fp8", tuple(range(32, 513, 32)), [c4_step(300 + s, cfg.vocab) for s in range(4)]
+
+
+def _barrier(dist):
+    import torch
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+
+
+def _max_over_ranks(dist, x):
+    if not dist:
+        return x
+    import torch
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def measure_batched(w, cfg, weights, local, rank, world, dist, steps, warmup, lanes=1):
+    """C2 / C3 / C4 through the public engine API on this rank's share of each
+    step (C4 shards its questions over the ranks by LPT; C2 / C3 run whole on
+    every rank).  Returns the measurement dict (every rank computes it; the
+    values are maxima over ranks)."""
+    from laya_b200.engine import B200Engine, request_from_items
+    from laya_b200.dispatcher import shard_for_rank, group_by_bucket
+    precision, buckets, steps_items = batched_plan(w, cfg)
+    lanes = max(1, lanes) if w == "c4" else 1   # C4 steps hold several bucket groups
+    eng = B200Engine(config=cfg, weights=weights, device=local, precision=precision, max_questions=64,
+                     max_options=4, max_graphs=512, sequence_buckets=buckets, lanes=lanes)
+    try:
+        plans = []
+        shard = w == "c4" and world > 1
+        for items in steps_items:
+            mine = shard_for_rank(items, world, rank, buckets) if shard else list(range(len(items)))
+            groups = group_by_bucket(items, mine, buckets, 64)
+            plans.append([request_from_items([items[i] for i in idx]) for _, idx in groups])
+        for plan in plans * max(1, warmup // len(plans)):     # captures every shape, then warm
             for req in plan:
-                eng._run_on(req, lane)
-
-    def barrier():
-        if dist:
-            dist.barrier()
-        torch.cuda.synchronize()
-
-    def max_over_ranks(x):
-        if not dist:
-            return x
-        t = torch.tensor([x], dtype=torch.float64, device="cuda")
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        return float(t.item())
-
-    # device time per step: the step's graphs replayed back to back with inputs resident
-    dev_ms = []
-    launches = 0  # kernels launched by the timed replays
-    for plan in plans:
-        t = 0.0
-        for req in plan:
-            eng._run_on(req, eng)                 # lane 0: its staging buffer now holds req
-            slot = eng.graphs[eng._graph_key(req)]
-            t += float(np.mean(eng.native.replay_device(slot, 5)))
-            launches += 5 * eng.native.kernel_count(slot)
-        dev_ms.append(t)
-    with ClockSampler(local) as clocks:
-        barrier()
-        t0 = time.perf_counter()
-        for k in range(args.steps):
-            for req in plans[k % len(plans)]:
-                eng.run_prepared(req)
-        wall = max_over_ranks(time.perf_counter() - t0)
-        barrier()
-    # serving lanes (C4): the step's bucket groups dispatched concurrently, one
-    # caller thread per lane; host wall clock over the steps
-    lanes_line = None
-    if lanes > 1:
-        from concurrent.futures import ThreadPoolExecutor
-        with ThreadPoolExecutor(max_workers=lanes) as pool:
+                eng._run_on(req, eng)
+        for lane in eng._lanes[1:]:                  # every lane holds every shape's graph
             for plan in plans:
-                list(pool.map(eng.run_prepared, plan))
-            barrier()
+                for req in plan:
+                    eng._run_on(req, lane)
+        # device time per step: the step's graphs replayed back to back with inputs resident
+        dev_ms, launches = [], 0
+        for plan in plans:
+            t = 0.0
+            for req in plan:
+                eng._run_on(req, eng)                 # lane 0: its staging buffer now holds req
+                slot = eng.graphs[eng._graph_key(req)]
+                t += float(np.mean(eng.native.replay_device(slot, 5)))
+                launches += 5 * eng.native.kernel_count(slot)
+            dev_ms.append(t)
+        with ClockSampler(local) as clocks:
+            _barrier(dist)
             t0 = time.perf_counter()
-            for k in range(args.steps):
-                list(pool.map(eng.run_prepared, plans[k % len(plans)]))
-            lanes_wall = max_over_ranks(time.perf_counter() - t0)
-            barrier()
-        lanes_line = {"lanes": lanes, "value": args.steps * sum(len(it) for it in steps_items) / len(steps_items)
-                      / lanes_wall, "unit": UNIT, "ms_per_step": 1000 * lanes_wall / args.steps,
-                      "timing": "host wall clock, bucket groups of a step on concurrent lanes (public API, "
-                                "host buffers)"}
+            for k in range(steps):
+                for req in plans[k % len(plans)]:
+                    eng.run_prepared(req)
+            wall = _max_over_ranks(dist, time.perf_counter() - t0)
+            _barrier(dist)
+        # serving lanes (C4): the step's bucket groups dispatched concurrently,
+        # one caller thread per lane; host wall clock over the steps
+        lanes_line = None
+        if lanes > 1:
+            from concurrent.futures import ThreadPoolExecutor
+            with ThreadPoolExecutor(max_workers=lanes) as pool:
+                for plan in plans:
+                    list(pool.map(eng.run_prepared, plan))
+                _barrier(dist)
+                t0 = time.perf_counter()
+                for k in range(steps):
+                    list(pool.map(eng.run_prepared, plans[k % len(plans)]))
+                lanes_wall = _max_over_ranks(dist, time.perf_counter() - t0)
+                _barrier(dist)
+            lanes_line = {"lanes": lanes,
+                          "value": steps * sum(len(it) for it in steps_items) / len(steps_items) / lanes_wall,
+                          "unit": UNIT, "ms_per_step": 1000 * lanes_wall / steps,
+                          "timing": "host wall clock, bucket groups of a step on concurrent lanes (public API, "
+                                    "host buffers)"}
+    finally:
+        eng.close()
     questions = sum(len(it) for it in steps_items) / len(steps_items)
-    dev_step = max_over_ranks(float(np.mean(dev_ms)))
-    value = questions / (dev_step / 1000.0)
-    e2e = args.steps * questions / wall
+    dev_step = _max_over_ranks(dist, float(np.mean(dev_ms)))
+    # C4 is sharded: the whole step's questions in the slowest rank's time;
+    # C2 / C3 run whole on every rank: world x questions
+    served = questions if shard else questions * world
+    value = served / (dev_step / 1000.0)
+    e2e = steps * served / wall
     flops = float(np.mean([encoder_flops(cfg, items) for items in steps_items]))
     d = json.loads((ROOT / "MEASURED_PEAKS.json").read_text()) if (ROOT / "MEASURED_PEAKS.json").exists() else {}
     bf16_peak = float(d.get("bf16_tflops", 1590.0))
-    peak = 2 * bf16_peak if precision == "fp8" else 4 * bf16_peak if precision == "nvfp4" else bf16_peak
-    achieved = flops / (dev_step / 1000.0) / 1e12 / world
+    mult = 2 if precision == "fp8" else 4 if precision == "nvfp4" else 1
+    peak = mult * bf16_peak
+    # per GPU: the step's FLOPs (C4: divided over the ranks) in the slowest rank's device time
+    achieved = flops * (served / questions) / world / (dev_step / 1000.0) / 1e12
+    return {"metric": "decisions/s", "value": value, "unit": UNIT, "n_gpus": world, "steps": steps,
+            "warmup": warmup, "ms_per_step": dev_step, "higher_is_better": True,
+            "scaling": "strong" if shard else "weak",
+            "dtype": {"fp8": "e4m3", "nvfp4": "e2m1"}[precision],
+            "config": {"workload": w, "precision": precision, "questions_per_step": questions,
+                       "buckets": list(buckets) if len(buckets) < 5 else "multiples of 32 up to 512",
+                       "parallelism": (f"LPT shards of each step over {world} ranks" if shard else
+                                       f"request-parallel replicas x{world}")},
+            "e2e": {"value": e2e, "unit": UNIT, "path": "B200Engine.run_prepared per bucket group"},
+            "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+                         "frac": achieved / peak, "flops_per_step": flops,
+                         "peak_source": f"{mult}x measured cuBLAS bf16 (MEASURED_PEAKS.json)"},
+            **({"serving_lanes": lanes_line} if lanes_line else {}),
+            "gpu_launches": launches, "clocks": clocks.summary()}
+
+
+def run_batched(args):
+    """--workload c2 / c3 / c4: one JSON line of that workload."""
+    rank, world, local, dist = dist_setup(args.gpus)
+    from laya_b200.config import LAYA
+    from laya_b200.weights import seeded_weights
+    weights = seeded_weights(LAYA, seed=0)
+    line = measure_batched(args.workload, LAYA, weights, local, rank, world, dist, args.steps, args.warmup,
+                           args.lanes)
     if rank == 0:
-        cs = clocks.summary()
-        line = {"metric": "decisions/s", "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
-                "warmup": args.warmup, "ms_per_step": dev_step, "higher_is_better": True, "scaling": "weak" if w != "c4" else "strong",
-                "vs_baseline": None, "dtype": {"fp8": "e4m3", "nvfp4": "e2m1"}[precision], "data": "synthetic",
-                "config": {"workload": w, "precision": precision, "questions_per_step": questions,
-                           "buckets": list(buckets) if len(buckets) < 5 else "multiples of 32 up to 512",
-                           "parallelism": f"request-parallel x{world}"},
-                "e2e": {"value": e2e, "unit": UNIT, "path": "B200Engine.run_prepared per bucket group"},
-                "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
-                             "frac": achieved / peak, "flops_per_step": flops,
-                             "peak_source": f"{'2x' if precision == 'fp8' else '4x' if precision == 'nvfp4' else '1x'} "
-                                            "measured cuBLAS bf16 (MEASURED_PEAKS.json)"},
-                **({"serving_lanes": lanes_line} if lanes_line else {}),
-                "gpu_launches": launches,
-                "clocks": cs}
+        line["vs_baseline"] = None
+        line["data"] = "synthetic"
         print(json.dumps(line), flush=True)
-    eng.close()
     if dist:
         dist.barrier()
         dist.destroy_process_group()
     return 0
+
+
+def reference_gpu(cfg, weights, local, steps, warmup):
+    """The reference's own path on this GPU: FastDecisionModel with its Triton
+    RoPE, each shape captured in a CUDA graph after three eager warm-ups on a
+    side stream, as BlackwellEngine._slot does (src/laya_blackwell/engine.py:
+    161-187); device time of back-to-back replays with inputs resident (CUDA
+    events), and end to end as BlackwellEngine.run_prepared runs it (pinned
+    host inputs copied into the graph's inputs, replay, outputs copied back).
+    FP8 uses the reference's replace_encoder_linears (FP8Linear)."""
+    import torch
+    from baseline import laya_net
+    from laya_b200.workload import synthetic_items, pack, mixed_kinds
+    dev = torch.device("cuda", local)
+    out = {"path": "baseline/_ref laya_blackwell.model.FastDecisionModel, Triton rope_qkv, torch.cuda.graph"}
+    cases = [("c1_bf16", "bf16", synthetic_items([64], ["noul"], seed=0, vocab=cfg.vocab), 1, 64, 2),
+             ("c3_bf16", "bf16", synthetic_items([512], ["choice"], seed=200, vocab=cfg.vocab), 1, 512, 4),
+             ("c1_fp8", "fp8", synthetic_items([64], ["noul"], seed=0, vocab=cfg.vocab), 1, 64, 2),
+             ("c2_fp8", "fp8", synthetic_items([96] * 16, mixed_kinds(16, 0), seed=100, vocab=cfg.vocab), 16, 96, 4)]
+    model = laya_net.build(cfg, weights, dev, rope="native")
+    fp8 = False
+    for name, precision, items, b, s, k in cases:
+        if precision == "fp8" and not fp8:
+            laya_net.import_reference("quantization").replace_encoder_linears(model)
+            fp8 = True
+        laya_net.use_rope("native")
+        host = {kk: torch.from_numpy(v).pin_memory() for kk, v in pack(items, b, s, k, cfg.pad_token_id).items()}
+        host["marker_mask"] = host["marker_mask"].bool()
+        unmasked = len(items) == b and all(len(it["ids"]) == s for it in items)
+        with torch.inference_mode():
+            inputs = {kk: v.to(dev) for kk, v in host.items()}
+            stream = torch.cuda.Stream(device=dev)
+            stream.wait_stream(torch.cuda.current_stream(dev))
+            with torch.cuda.stream(stream):
+                for _ in range(3):
+                    model(**inputs, global_attention_unmasked=unmasked)
+            torch.cuda.current_stream(dev).wait_stream(stream)
+            torch.cuda.synchronize(dev)
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph, stream=stream):
+                outputs = model(**inputs, global_attention_unmasked=unmasked)
+            for _ in range(warmup):
+                graph.replay()
+            torch.cuda.synchronize(dev)
+            n = steps if s <= 96 else max(10, steps // 8)
+            evs = [torch.cuda.Event(enable_timing=True) for _ in range(n + 1)]
+            cur = torch.cuda.current_stream(dev)
+            evs[0].record(cur)
+            for i in range(n):
+                graph.replay()
+                evs[i + 1].record(cur)
+            torch.cuda.synchronize(dev)
+            ms = [evs[i].elapsed_time(evs[i + 1]) for i in range(n)]
+            out_host = [torch.empty_like(o, device="cpu").pin_memory() for o in outputs]
+            t0 = time.perf_counter()
+            for _ in range(n):
+                for kk, v in host.items():
+                    inputs[kk].copy_(v, non_blocking=True)
+                graph.replay()
+                for o, h in zip(outputs, out_host):
+                    h.copy_(o, non_blocking=True)
+                torch.cuda.synchronize(dev)
+            e2e_s = (time.perf_counter() - t0) / n
+            del graph
+        dev_ms = float(np.mean(ms))
+        out[name] = {"precision": precision, "shape": [b, s, k], "questions": len(items), "ms_per_step": dev_ms,
+                     "p50_ms": float(np.median(ms)), "value": len(items) / (dev_ms / 1000.0), "unit": UNIT,
+                     "e2e": {"value": len(items) / e2e_s, "unit": UNIT, "ms_per_step": 1000 * e2e_s},
+                     "steps": n}
+    del model
+    torch.cuda.empty_cache()
+    return out
 
 
 def main():
@@ -402,9 +543,11 @@ def main():
     import torch
     from laya_b200.config import LAYA
     from laya_b200.engine import B200Engine, request_from_items
+    from laya_b200.weights import seeded_weights
     cfg = LAYA
-    eng = B200Engine(config=cfg, device=local, precision=args.precision, max_questions=1, max_options=2,
-                     max_graphs=2, lanes=max(1, args.lanes), token_tables=args.token_tables)
+    weights = seeded_weights(cfg, seed=0)
+    eng = B200Engine(config=cfg, weights=weights, device=local, precision=args.precision, max_questions=1,
+                     max_options=2, max_graphs=2, lanes=max(1, args.lanes), token_tables=args.token_tables)
     items, inp = workload(cfg, seed=rank)
     prepared = request_from_items(items)
     logits, act, meta = eng._run_on(prepared, eng)  # lane 0: captures the graph, inputs now resident
@@ -493,8 +636,25 @@ def main():
             if line.startswith("traffic_bytes_per_launch:"):
                 traffic = float(line.split(":", 1)[1])
 
+    eng.close()
+
+    # ---- the other BASELINE configs, bounded (every rank takes part)
+    configs = {}
+    if not args.no_configs:
+        for w in ("c2", "c3", "c4"):
+            n = args.config_steps if w != "c4" else max(4, args.config_steps // 4)
+            configs[w] = measure_batched(w, cfg, weights, local, rank, world, dist, n, 3, lanes=1)
+
+    ref_gpu = None
+    if rank == 0 and not args.no_reference_gpu:
+        try:
+            ref_gpu = reference_gpu(cfg, weights, local, min(args.steps, 200), 3)
+        except Exception as exc:  # noqa: BLE001 - reported in the line, not fatal
+            ref_gpu = {"unavailable": f"{type(exc).__name__}: {exc}"[:300]}
+    _barrier(dist)
+
     if rank == 0:
-        base = cpu_baseline(cfg, args.cpu_seconds, args.precision)
+        base = cpu_baseline(cfg, args.cpu_seconds, args.precision, weights=weights)
         cs = clocks.summary()
         line = {
             "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
@@ -523,9 +683,10 @@ def main():
             "gpu_launches": kernels * args.steps,
             "kernels_per_forward": kernels,
             "clocks": cs,
+            **({"configs": configs} if configs else {}),
+            **({"reference_gpu": ref_gpu} if ref_gpu else {}),
         }
         print(json.dumps(line), flush=True)
-    eng.close()
     if dist:
         dist.barrier()
         dist.destroy_process_group()

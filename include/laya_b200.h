@@ -108,6 +108,17 @@ LAYA_B200_API int laya_b200_run(laya_b200_engine* e, int slot, const int64_t* in
 LAYA_B200_API int laya_b200_replay_device(laya_b200_engine* e, int slot, int iterations, int kernel_mask,
                                           float* ms_each);
 
+/* Test hook with no counterpart in the reference (failure detection): the
+ * next laya_b200_run on this engine enqueues its forward without a graph, and
+ * the first generic projection launch in it never loads its first pipeline
+ * stage and limits each of its waits to wait_limit_us microseconds (1 ..
+ * 1,000,000).  Nothing completes that stage's barrier, so the kernel's
+ * bounded waits run out: it records a timeout in the engine's status word,
+ * drains its own copies, frees its tensor memory and returns, and the run
+ * fails with a "device-side wait timed out" error.  The engine stays usable;
+ * later runs are unaffected. */
+LAYA_B200_API int laya_b200_test_withhold_stage(laya_b200_engine* e, int wait_limit_us);
+
 /* Number of kernels one forward of the slot launches. */
 LAYA_B200_API int laya_b200_kernel_count(laya_b200_engine* e, int slot, int* count);
 

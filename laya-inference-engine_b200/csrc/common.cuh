@@ -68,15 +68,21 @@ DEVI bool mbar_try(uint32_t addr, uint32_t parity) {
 }
 
 // Wait for the phase with the given parity to complete.  Returns false after
-// kWaitLimitNs without completion.
-DEVI bool mbar_wait(uint64_t* bar, uint32_t parity) {
+// `limit_ns` (default kWaitLimitNs) without completion.
+DEVI bool mbar_wait(uint64_t* bar, uint32_t parity, uint64_t limit_ns = kWaitLimitNs) {
   const uint32_t addr = smem_u32(bar);
   if (mbar_try(addr, parity)) return true;
   const uint64_t t0 = globaltimer();
   while (true) {
     if (mbar_try(addr, parity)) return true;
-    if (globaltimer() - t0 > kWaitLimitNs) return false;
+    if (globaltimer() - t0 > limit_ns) return false;
   }
+}
+
+// Wait limit of a launch: its parameter block's override in microseconds, or
+// the default.
+DEVI uint64_t wait_limit(uint32_t override_us) {
+  return override_us ? (uint64_t)override_us * 1000ull : kWaitLimitNs;
 }
 
 // ---------------------------------------------------------------- TMA

@@ -250,6 +250,10 @@ struct laya_b200_engine {
   // The slot whose inputs the device staging buffer holds (set by run): a
   // kernels-only replay of another slot would read another shape's layout.
   int inputs_slot = -1;
+  // Test hook (laya_b200_test_withhold_stage): wait limit in microseconds for
+  // the next run's first generic projection, whose first stage is withheld;
+  // 0 = not armed.
+  uint32_t test_withhold_us = 0;
 
   std::vector<cudaEvent_t> timing_events;
 };
@@ -345,6 +349,7 @@ struct Fwd {
   int mask = kCatAll;  // enqueue only kernels of these categories
   bool first = true;
   bool eager_check = false;  // synchronise and check after every launch
+  uint32_t test_withhold_us = 0;  // test hook for the next generic projection launch
 
   bool on(int cat) const { return (mask & cat) != 0; }
   bool pdl() {
@@ -403,6 +408,11 @@ struct Fwd {
       p.rope_cols = 2 * (w.N / 3);
     }
     if (ln_stats) p.ln_stats = e->lnst;
+    if (test_withhold_us) {  // test hook: this launch's first stage is never loaded
+      p.test_withhold = 1;
+      p.wait_limit_us = test_withhold_us;
+      test_withhold_us = 0;
+    }
     count(launch_gemm(w.kind, w.map, xmap, omap, p, bn, split, st, pdl()), "gemm launch");
     return rotated;
   }
@@ -1390,12 +1400,16 @@ int laya_b200_run(laya_b200_engine* e, int slot, const int64_t* input_ids, const
     // The copy below overwrites the staging buffer with this slot's layout:
     // until it has completed, no slot's inputs are known to be resident.
     e->inputs_slot = -1;
-    if (e->sync_check) {
+    const uint32_t withhold_us = e->test_withhold_us;
+    e->test_withhold_us = 0;
+    if (e->sync_check || withhold_us) {
       ck(cudaMemcpyAsync(e->d_in, e->h_in, L.words * 4, cudaMemcpyHostToDevice, e->stream), "H2D");
       e->launches = 0;
       Fwd f{e, e->stream, kCatAll};
-      f.eager_check = true;
+      f.eager_check = e->sync_check;
+      f.test_withhold_us = withhold_us;
       f.run(sl.sh);
+      if (withhold_us && f.test_withhold_us) fail("test hook: the forward has no generic projection launch");
       ck(cudaMemcpyAsync(e->h_out, e->d_out, L.out_words * 4, cudaMemcpyDeviceToHost, e->stream), "D2H");
     } else {
       ck(cudaGraphLaunch(sl.io_exec, e->stream), "graph launch");
@@ -1437,6 +1451,13 @@ int laya_b200_replay_device(laya_b200_engine* e, int slot, int iterations, int k
       e->status_host[0] = 0;
       fail("a device-side wait timed out during replay");
     }
+  });
+}
+
+int laya_b200_test_withhold_stage(laya_b200_engine* e, int wait_limit_us) {
+  return guard(e, [&] {
+    if (wait_limit_us < 1 || wait_limit_us > 1000000) fail("wait_limit_us must be in [1, 1000000]");
+    e->test_withhold_us = (uint32_t)wait_limit_us;
   });
 }
 

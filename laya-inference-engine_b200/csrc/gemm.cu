@@ -98,22 +98,25 @@ __global__ void __launch_bounds__(BN >= 128 ? 256 : 128, BN == 128 ? 2 : 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
+  const uint64_t limit = wait_limit(p.wait_limit_us);
   int issued = 0;  // producer: loads issued (for the drain on failure)
   if (tid == 0) {
     const uint64_t pol_w = policy_evict_first();
     const uint64_t pol_x = policy_evict_last();
     const int pre = nkb < STAGES ? nkb : STAGES;
     for (int i = 0; i < pre; ++i) {
+      if (i + 1 == p.test_withhold) continue;  // test hook: nothing completes this stage
       mbar_expect_tx(&full[i], C::STAGE_BYTES);
       tma_load_2d(sA + i * C::A_BYTES, &wmap, &full[i], (kb0 + i) * C::K_ELEMS, tile_n * 128, pol_w);
     }
     griddep_wait();
     for (int i = 0; i < pre; ++i)
-      tma_load_2d(sB + i * C::B_BYTES, &xmap, &full[i], (kb0 + i) * C::K_ELEMS, tile_m * BN, pol_x);
+      if (i + 1 != p.test_withhold)
+        tma_load_2d(sB + i * C::B_BYTES, &xmap, &full[i], (kb0 + i) * C::K_ELEMS, tile_m * BN, pol_x);
     issued = pre;
     for (int i = pre; i < nkb; ++i) {
       const int s = i % STAGES;
-      if (!mbar_wait(&empty[s], ((i / STAGES) - 1) & 1)) {
+      if (!mbar_wait(&empty[s], ((i / STAGES) - 1) & 1, limit)) {
         record_status(p.status, kStatusGemmEmptyTimeout);
         atomicExch(failed, 1u);
         break;
@@ -127,7 +130,7 @@ __global__ void __launch_bounds__(BN >= 128 ? 256 : 128, BN == 128 ? 2 : 1)
     const uint32_t idesc = KIND == kKindBf16 ? idesc_bf16(128, BN) : idesc_e4m3(128, BN);
     for (int i = 0; i < nkb; ++i) {
       const int s = i % STAGES;
-      if (!mbar_wait(&full[s], (i / STAGES) & 1)) {
+      if (!mbar_wait(&full[s], (i / STAGES) & 1, limit)) {
         record_status(p.status, kStatusGemmFullTimeout);
         atomicExch(failed, 1u);
         break;
@@ -153,7 +156,7 @@ __global__ void __launch_bounds__(BN >= 128 ? 256 : 128, BN == 128 ? 2 : 1)
 
   // ---- epilogue: TMEM -> shared partial [BN][128] fp32 -> cluster reduction
   griddep_wait();
-  if (!mbar_wait(done, 0)) {
+  if (!mbar_wait(done, 0, limit)) {
     record_status(p.status, kStatusGemmDoneTimeout);
     atomicExch(failed, 1u);
   }
@@ -167,7 +170,7 @@ __global__ void __launch_bounds__(BN >= 128 ? 256 : 128, BN == 128 ? 2 : 1)
   // ---- teardown: drain copies still in flight after a failure, free TMEM
   if (tid == 0 && *failed) {
     for (int i = (issued > STAGES ? issued - STAGES : 0); i < issued; ++i)
-      mbar_wait(&full[i % STAGES], (i / STAGES) & 1);
+      mbar_wait(&full[i % STAGES], (i / STAGES) & 1, limit);
   }
   tc_fence_before();
   __syncthreads();

@@ -83,6 +83,12 @@ struct GemmParams {
   // row, (mean, sum of squared deviations) over the tile, at
   // [token * (N / 128) + tile].
   float2* ln_stats;
+  // Test hooks (zero in every normal launch): wait_limit_us shortens every
+  // bounded wait of the launch; test_withhold = 1 + the index of a prefetched
+  // pipeline stage whose loads are never issued, so the waits on it run out
+  // (gemm_kernel only).
+  uint32_t wait_limit_us;
+  int test_withhold;
 };
 
 // LayerNorm applied by a projection to its fp32 input rows while building the

@@ -16,7 +16,8 @@ EXPORTS = ("laya_b200_create", "laya_b200_set_weight", "laya_b200_finalize", "la
            "laya_b200_build_token_tables",
            "laya_b200_capture",
            "laya_b200_release", "laya_b200_run", "laya_b200_replay_device", "laya_b200_kernel_count",
-           "laya_b200_read_buffer", "laya_b200_tail_noalloc", "laya_b200_last_error", "laya_b200_destroy")
+           "laya_b200_read_buffer", "laya_b200_tail_noalloc", "laya_b200_test_withhold_stage",
+           "laya_b200_last_error", "laya_b200_destroy")
 
 
 class Config(ctypes.Structure):
@@ -72,6 +73,7 @@ def load():
         "laya_b200_kernel_count": (I, [P, I, ctypes.POINTER(I)]),
         "laya_b200_read_buffer": (I, [P, ctypes.c_char_p, P, ctypes.c_size_t]),
         "laya_b200_tail_noalloc": (I, [ctypes.POINTER(TailArgs), P]),
+        "laya_b200_test_withhold_stage": (I, [P, I]),
         "laya_b200_last_error": (ctypes.c_char_p, [P]),
         "laya_b200_destroy": (I, [P]),
     }

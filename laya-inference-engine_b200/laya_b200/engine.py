@@ -121,6 +121,14 @@ class NativeForward:
         _lib.check(self.lib, self.handle, st, f"read_buffer({name})")
         return out
 
+    def test_withhold_stage(self, wait_limit_us=1000):
+        """Test hook (failure detection): the next run() enqueues its forward
+        without a graph and its first generic projection never loads its first
+        pipeline stage, so that launch's bounded waits (limited to
+        `wait_limit_us`) run out and the run raises RuntimeError."""
+        _lib.check(self.lib, self.handle, self.lib.laya_b200_test_withhold_stage(self.handle, int(wait_limit_us)),
+                   "test_withhold_stage")
+
     def build_token_tables(self):
         """Embedding-norm and layer-0 QKV rows of every token id on the device
         (slots captured afterwards start with one gather)."""

@@ -1,6 +1,7 @@
-"""bench.py's reference arm (the CPU oracle port of the reference forward,
-timed on this host's cores) prints one JSON line with the benchmark contract's
-keys; it needs no GPU."""
+"""bench.py's reference arm (the reference's own CPU forward from the offline
+install in baseline/_ref, or the CPU oracle port of it when the reference is
+not installed, timed on this host's cores) prints one JSON line with the
+benchmark contract's keys; it needs no GPU."""
 import json
 import subprocess
 import sys
@@ -26,5 +27,8 @@ def test_reference_arm_prints_the_contract_line():
     assert line["value"] > 0 and abs(line["e2e"]["value"] - line["value"]) < 1e-9
     assert line["e2e"]["h2d_bytes_per_step"] == 0 and line["e2e"]["d2h_bytes_per_step"] == 0
     base = line["cpu_baseline"]
-    assert base["kind"] == "port" and base["cores"] >= 1 and base["value"] == line["value"]
+    sys.path.insert(0, str(ROOT))
+    from baseline import laya_net
+    want = "reference" if laya_net.reference_src() is not None else "port"
+    assert base["kind"] == want and base["cores"] >= 1 and base["value"] == line["value"]
     assert line["config"]["workload"].startswith("C1")

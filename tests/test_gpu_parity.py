@@ -71,6 +71,8 @@ def compare(logits, act, ref_logits, ref_act, mm, tol, label):
 
 @pytest.mark.parametrize("path", sorted(GOLDEN.glob("*.npz")), ids=lambda p: p.stem)
 def test_bf16_matches_reference_golden(path):
+    """Every golden case (the reference's own outputs): C1 full and padded,
+    b4 x s96 mixed, C2's 16 x 96 shape, s512 partial and full, tiny networks."""
     z = np.load(path)
     name = str(z["config"])
     inputs = {k: z[k] for k in KEYS}
@@ -111,6 +113,27 @@ def test_invalid_inputs_are_rejected_on_the_host():
     with pytest.raises(RuntimeError, match="marker_pos"):
         nf.run(slot, bad)
     nf.run(slot, inp)  # the engine stays usable
+
+
+@pytest.mark.parametrize("precision,golden", [
+    ("fp8", "laya_c1_noul_full"), ("fp8", "laya_c2_b16_s96"),
+    ("nvfp4", "laya_c1_noul_full"), ("nvfp4", "laya_c3_s512_full"),
+])
+def test_low_precision_meets_the_tolerance_against_the_reference_bf16(precision, golden):
+    """north_star's criterion: FP8 / NVFP4 logits and act within 6e-2 / 1.5e-1
+    max-abs of the reference's own bf16 path (the golden outputs), and the
+    same decision wherever the reference's top-2 margin exceeds the tolerance;
+    the overall decision agreement rate is printed."""
+    z = np.load(GOLDEN / f"{golden}.npz")
+    inputs = {k: z[k] for k in KEYS}
+    b, s = inputs["input_ids"].shape
+    k = inputs["marker_pos"].shape[1]
+    nf = engine_for("laya", precision)
+    slot = nf.capture(b, s, k, bool(z["unmasked"]))
+    logits, act = nf.run(slot, inputs)
+    n = int(z["n_items"])
+    compare(logits[:n], act[:n], z["ref_logits"][:n], z["ref_act"][:n], inputs["marker_mask"][:n],
+            TOL[precision], f"{precision} {golden} vs reference bf16")
 
 
 @pytest.mark.parametrize("name,lengths,s,k", [
