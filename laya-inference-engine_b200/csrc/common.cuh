@@ -21,6 +21,13 @@ enum : uint32_t {
   kStatusAttnTimeout = 4,
 };
 
+// e4m3 row scale = max(amax * fl(1/448), 1e-12).  The reference's FP8 path
+// multiplies by the fp32 reciprocal of 448 rather than dividing (PyTorch's CUDA
+// division of a tensor by a scalar and Triton's division by a constant both
+// lower to that product), which differs from amax / 448 in the last bit for
+// some inputs; the golden vectors of its FP8Linear pin this form.
+constexpr float kInvE4m3Max = 1.0f / 448.0f;
+
 // Every spin on an mbarrier gives up after this many nanoseconds, records an
 // error in the status word and lets the kernel unwind.
 constexpr uint64_t kWaitLimitNs = 2000000000ull;

@@ -93,7 +93,7 @@ DEVI void norm_row(const NormParams& p, int row, int lane) {
   }
   if (p.out_fp8) {
     amax = warp_max(amax);
-    const float scale = fmaxf(amax / 448.0f, 1e-12f), inv = 1.0f / scale;
+    const float scale = fmaxf(amax * kInvE4m3Max, 1e-12f), inv = 1.0f / scale;
     uint8_t* dst = p.out_fp8 + (size_t)row * p.d;
 #pragma unroll
     for (int i = 0; i < NV; ++i) {
@@ -230,7 +230,7 @@ DEVI void norm_row_cta(const NormParams& p, int row, float* red) {
   if (!p.out_fp8 && !p.out_x4) return;
   amax = cta_max(amax, red, nw);
   if (p.out_fp8) {
-    const float scale = fmaxf(amax / 448.0f, 1e-12f), inv = 1.0f / scale;
+    const float scale = fmaxf(amax * kInvE4m3Max, 1e-12f), inv = 1.0f / scale;
     uint32_t w[2];
 #pragma unroll
     for (int j = 0; j < 2; ++j) {

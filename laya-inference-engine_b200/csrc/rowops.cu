@@ -65,7 +65,7 @@ __global__ void __launch_bounds__(128) quant_fp8_kernel(const QuantParams p) {
   if (lane == 0) s_max[warp] = amax;
   __syncthreads();
   amax = fmaxf(fmaxf(s_max[0], s_max[1]), fmaxf(s_max[2], s_max[3]));
-  const float scale = fmaxf(amax / 448.0f, 1e-12f), inv = 1.0f / scale;
+  const float scale = fmaxf(amax * kInvE4m3Max, 1e-12f), inv = 1.0f / scale;
   uint8_t* dst = p.q + (size_t)row * p.k;
 #pragma unroll
   for (int i = 0; i < MAXC; ++i) {
@@ -209,7 +209,7 @@ __global__ void __launch_bounds__(256) pack_fp8_rows_kernel(const __nv_bfloat16*
   float amax = 0.f;
   for (int c = lane; c < k; c += 32) amax = fmaxf(amax, fabsf(__bfloat162float(src[c])));
   amax = warp_max(amax);
-  const float s = fmaxf(amax / 448.0f, 1e-12f);
+  const float s = fmaxf(amax * kInvE4m3Max, 1e-12f);
   for (int c = lane * 2; c < k; c += 64) {
     const float a = fminf(fmaxf(__bfloat162float(src[c]) / s, -448.f), 448.f);
     const float b = fminf(fmaxf(__bfloat162float(src[c + 1]) / s, -448.f), 448.f);

@@ -61,11 +61,17 @@ def e4m3(x):
     return x.to(torch.float8_e4m3fn).to(torch.float32)
 
 
+# fp32 reciprocal of 448: the reference computes amax / 448 as amax * fl(1/448)
+# (PyTorch's CUDA tensor-by-scalar division and Triton's division by a constant
+# both lower to that product); pinned by tests/golden/fp8_linear.
+INV_E4M3_MAX = torch.tensor(1.0, dtype=torch.float32) / torch.tensor(E4M3_MAX, dtype=torch.float32)
+
+
 def fp8_quantize_rows(x):
     """quantization.py:20-29 (_quantize_rows) and :69-73 (weights): per-row
-    scale = max(amax/448, 1e-12), values clamp(x/scale, +-448) -> e4m3."""
+    scale = max(amax * fl(1/448), 1e-12), values clamp(x/scale, +-448) -> e4m3."""
     amax = x.abs().amax(dim=-1, keepdim=True)
-    scale = torch.clamp(amax / E4M3_MAX, min=FP8_MIN_SCALE)
+    scale = torch.clamp(amax * INV_E4M3_MAX, min=FP8_MIN_SCALE)
     q = e4m3(torch.clamp(x / scale, -E4M3_MAX, E4M3_MAX))
     return q, scale
 

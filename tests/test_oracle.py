@@ -1,6 +1,9 @@
-"""The CPU oracle against the reference's own forward (golden fixtures) and the
+"""The CPU oracle against the reference's own forward (golden fixtures), the
+reference's own FP8 linear (golden vectors made on a B200) and the
 reference's known-answer kernel tests.  CPU only."""
 import functools
+import hashlib
+import importlib.util
 from pathlib import Path
 
 import numpy as np
@@ -48,6 +51,40 @@ def test_oracle_matches_reference_forward(path, bf16_gemm):
     margins = O.top2_margin(ref_l, mm)
     decided = margins > 2e-2
     assert O.decision_agreement(ref_l[decided], logits[:n][decided], mm[decided]) == 1.0
+
+
+def _fp8_case_inputs():
+    spec = importlib.util.spec_from_file_location("make_fp8_golden", GOLDEN / "make_fp8_golden.py")
+    mod = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mod)
+    return mod.fp8_case_inputs
+
+
+@pytest.mark.parametrize("path", sorted((GOLDEN / "fp8_linear").glob("*.npz")), ids=lambda p: p.stem)
+def test_fp8_oracle_matches_the_reference_fp8_linear(path):
+    """The FP8 oracle against the reference's FP8Linear run on a B200
+    (tests/golden/make_fp8_golden.py: Triton _quantize_rows + torch._scaled_mm,
+    quantization.py:20-107): activation e4m3 codes and row scales bit-exact,
+    weight row scales bit-exact and weight codes identical (digest), and the
+    bf16 outputs within one bf16 rounding of the fp32 sums (the reference's
+    GEMM accumulates in another order)."""
+    z = np.load(path)
+    m, n, k = int(z["m"]), int(z["n"]), int(z["k"])
+    x, w = _fp8_case_inputs()(m, n, k, int(z["seed"]), str(z["kind"]))
+    xq, xs = O.fp8_quantize_rows(x)
+    codes = xq.to(torch.float8_e4m3fn).view(torch.uint8).numpy()
+    assert np.array_equal(codes, z["x_codes"])
+    assert np.array_equal(xs[:, 0].numpy(), z["x_scale"])
+    wq, ws = O.fp8_quantize_rows(w)
+    assert np.array_equal(ws[:, 0].numpy(), z["w_scale"])
+    wcodes = wq.to(torch.float8_e4m3fn).view(torch.uint8).numpy()
+    assert hashlib.sha256(wcodes.tobytes()).hexdigest() == str(z["w_codes_sha256"])
+    y = O.encoder_linear(x, w, "fp8", {}, "case").numpy()
+    ref = (z["y"].astype(np.uint32) << 16).view(np.float32)
+    exact = (((xq @ wq.T) * xs * ws.T)).numpy()           # fp32 sums before the bf16 rounding
+    ulp = np.abs(exact) * 2.0 ** -7 + 1e-30                 # one bf16 step at the value
+    assert np.all(np.abs(y - ref) <= ulp), float(np.abs(y - ref).max())
+    assert (y == ref).mean() > 0.99
 
 
 @pytest.mark.parametrize("fp32", [True])
