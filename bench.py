@@ -353,7 +353,7 @@ def measure_batched(w, cfg, weights, local, rank, world, dist, steps, warmup, la
     every rank).  Returns the measurement dict (every rank computes it; the
     values are maxima over ranks)."""
     from laya_b200.engine import B200Engine, request_from_items
-    from laya_b200.dispatcher import shard_for_rank, group_by_bucket
+    from laya_b200.dispatcher import shard_groups, group_by_bucket
     precision, buckets, steps_items = batched_plan(w, cfg)
     lanes = max(1, lanes) if w == "c4" else 1   # C4 steps hold several bucket groups
     eng = B200Engine(config=cfg, weights=weights, device=local, precision=precision, max_questions=64,
@@ -362,8 +362,9 @@ def measure_batched(w, cfg, weights, local, rank, world, dist, steps, warmup, la
         plans = []
         shard = w == "c4" and world > 1
         for items in steps_items:
-            mine = shard_for_rank(items, world, rank, buckets) if shard else list(range(len(items)))
-            groups = group_by_bucket(items, mine, buckets, 64)
+            # C4 under torchrun: this rank's LPT share of the step's bucket groups
+            groups = shard_groups(items, world, buckets, 64)[rank] if shard else \
+                group_by_bucket(items, list(range(len(items))), buckets, 64)
             plans.append([request_from_items([items[i] for i in idx]) for _, idx in groups])
         for plan in plans * max(1, warmup // len(plans)):     # captures every shape, then warm
             for req in plan:
@@ -431,7 +432,7 @@ def measure_batched(w, cfg, weights, local, rank, world, dist, steps, warmup, la
             "dtype": {"fp8": "e4m3", "nvfp4": "e2m1"}[precision],
             "config": {"workload": w, "precision": precision, "questions_per_step": questions,
                        "buckets": list(buckets) if len(buckets) < 5 else "multiples of 32 up to 512",
-                       "parallelism": (f"LPT shards of each step over {world} ranks" if shard else
+                       "parallelism": (f"LPT shards of each step's bucket groups over {world} ranks" if shard else
                                        f"request-parallel replicas x{world}")},
             "e2e": {"value": e2e, "unit": UNIT, "path": "B200Engine.run_prepared per bucket group"},
             "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",

@@ -8,10 +8,12 @@ CUDA graphs and pinned buffers (one ``B200Engine`` per device, driven by its
 own worker thread: ctypes releases the GIL inside the native forward), and
 independent questions are partitioned across GPUs:
 
-* each question is priced at its bucketed token count (sequence bucket x 1);
-* questions are assigned longest-first to the least-loaded GPU (LPT);
-* on each GPU, questions that share a sequence bucket run as one batched
-  forward (batch padded to a power of two, as ``BlackwellEngine._shape``).
+* questions that share a sequence bucket form one batched forward (at most
+  ``max_batch``, batch padded to a power of two, as ``BlackwellEngine._shape``);
+* each group is priced at its padded tokens plus a fixed per-forward cost
+  (``group_cost``), and whole groups are assigned longest-first to the
+  least-loaded GPU (LPT), so a GPU runs a few full batches rather than many
+  one-question forwards.
 
 There is no collective anywhere: results return to the caller's thread.
 Failure handling is on the host: a worker that raises, or that has not
@@ -125,14 +127,15 @@ class B200Dispatcher:
                 alive = [d for d in self.devices if self.healthy[d]]
             if not alive:
                 raise RuntimeError(f"no healthy GPU left; {len(pending)} questions unserved: {errors}")
-            costs = [bucket_of(len(items[i]["ids"]), self.buckets) for i in pending]
-            shards = lpt_partition(costs, len(alive))
+            # whole bucket groups per GPU (LPT by estimated forward cost)
+            groups = split_for_balance(group_by_bucket(items, pending, self.buckets, self.max_batch), len(alive))
+            shards = lpt_partition([group_cost(b, len(g)) for b, g in groups], len(alive))
             futs = {}
             for d, shard in zip(alive, shards):
-                idx = [pending[j] for j in shard]
+                batches = [groups[j] for j in shard]
+                idx = sorted(i for _, g in batches for i in g)
                 if idx:
-                    fut = self.pools[d].submit(self._run_batches, d, items,
-                                               group_by_bucket(items, idx, self.buckets, self.max_batch))
+                    fut = self.pools[d].submit(self._run_batches, d, items, batches)
                     self.inflight[d] = fut
                     futs[d] = (idx, fut)
             # one deadline for the whole round, however many GPUs take part
@@ -203,6 +206,47 @@ def shard_for_rank(items, world, rank, buckets=tuple(range(32, 513, 32))):
     """The items one rank of a multi-process job serves (same LPT on every rank)."""
     costs = [bucket_of(len(it["ids"]), buckets) for it in items]
     return lpt_partition(costs, world)[rank]
+
+
+# Fixed cost of one batched forward in token-equivalents: a short forward is
+# bound by its dependent launches, not by its tokens (a 1 x 64 bf16 forward
+# takes as long as ~2k tokens of batched FP8 work on a B200).
+FORWARD_OVERHEAD_TOKENS = 2048
+
+
+def group_cost(bucket, batch):
+    """Estimated cost of one bucket group: padded tokens plus the fixed
+    per-forward overhead (the batch pads to a power of two, as
+    BlackwellEngine._shape does)."""
+    padded = 1 << (batch - 1).bit_length()
+    return bucket * padded + FORWARD_OVERHEAD_TOKENS
+
+
+def shard_groups(items, world, buckets=tuple(range(32, 513, 32)), max_batch=64):
+    """Whole bucket groups per rank: every rank forms the same groups (by
+    sequence bucket, at most max_batch each) and takes its LPT share of them
+    by group_cost, so a rank runs a few full batches rather than many
+    one-question forwards.  Returns, per rank, the list of (bucket, indices)."""
+    groups = split_for_balance(group_by_bucket(items, list(range(len(items))), buckets, max_batch), world)
+    costs = [group_cost(b, len(idx)) for b, idx in groups]
+    return [[groups[g] for g in part] for part in lpt_partition(costs, world)]
+
+
+def split_for_balance(groups, parts):
+    """Split the most expensive group (at its largest power of two below its
+    size, so neither half pads) while it costs more than an even share of the
+    work over `parts` GPUs; deterministic.  One GPU keeps the groups whole."""
+    groups = list(groups)
+    if parts <= 1:
+        return groups
+    while True:
+        costs = [group_cost(b, len(idx)) for b, idx in groups]
+        worst = max(range(len(groups)), key=lambda g: (costs[g], -g))
+        bucket, idx = groups[worst]
+        if len(idx) == 1 or costs[worst] <= sum(costs) / parts:
+            return groups
+        half = 1 << ((len(idx) - 1).bit_length() - 1)
+        groups[worst:worst + 1] = [(bucket, idx[:half]), (bucket, idx[half:])]
 
 
 def c4_step(seed, vocab, questions=64, lo=32, hi=512):

@@ -9,7 +9,8 @@ import pytest
 import torch.distributed as dist
 import torch.multiprocessing as mp
 
-from laya_b200.dispatcher import B200Dispatcher, lpt_partition, group_by_bucket, shard_for_rank, c4_step, bucket_of
+from laya_b200.dispatcher import (B200Dispatcher, lpt_partition, group_by_bucket, shard_for_rank, shard_groups,
+                                  group_cost, c4_step, bucket_of)
 
 
 class FakeEngine:
@@ -159,11 +160,29 @@ def test_c4_step_is_seeded():
     assert all(32 <= len(x["ids"]) <= 512 for x in a)
 
 
+def test_group_sharding_is_complete_and_balanced():
+    """Whole bucket groups per rank (what bench.py's C4 leg and the dispatcher
+    use): every question exactly once, groups never split, loads within one
+    group's cost of each other, the same answer on every call."""
+    items = c4_step(7, 1000)
+    for world in (1, 2, 4, 8):
+        shards = shard_groups(items, world)
+        assert len(shards) == world
+        flat = sorted(i for shard in shards for _, idx in shard for i in idx)
+        assert flat == list(range(len(items)))
+        loads = [sum(group_cost(b, len(idx)) for b, idx in shard) for shard in shards]
+        biggest = max(group_cost(b, len(idx)) for b, idx in group_by_bucket(items, list(range(64)),
+                                                                          tuple(range(32, 513, 32)), 64))
+        assert max(loads) - min(loads) <= biggest
+        assert shard_groups(items, world) == shards
+    assert group_cost(64, 1) == 64 + 2048 and group_cost(96, 5) == 96 * 8 + 2048
+
+
 def _rank_main(rank, world, port, items, q):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     dist.init_process_group("gloo", rank=rank, world_size=world)
     import torch
-    mine = shard_for_rank(items, world, rank)
+    mine = sorted(i for _, idx in shard_groups(items, world)[rank] for i in idx)
     gathered = [None] * world
     dist.all_gather_object(gathered, mine)
     t = torch.tensor([float(rank + 1)])
@@ -187,6 +206,6 @@ def test_two_rank_sharding_over_gloo():
         assert p.exitcode == 0
     flat = sorted(i for shard in gathered for i in shard)
     assert flat == list(range(len(items))) and tmax == 2.0
-    costs = [bucket_of(len(it["ids"]), tuple(range(32, 513, 32))) for it in items]
-    loads = [sum(costs[i] for i in s) for s in gathered]
-    assert abs(loads[0] - loads[1]) <= 512
+    # the two ranks computed their shares independently and agree on the split
+    want = [sorted(i for _, idx in shard for i in idx) for shard in shard_groups(items, 2)]
+    assert gathered == want
