@@ -242,3 +242,72 @@ def test_lanes_serve_concurrent_callers():
     engine.close()
     with pytest.raises(RuntimeError, match="closed"):
         engine.run_prepared(prepared)
+
+
+def test_predict_warmup_and_system_one_follow_the_reference_contract(monkeypatch):
+    """predict = prepare -> run_prepared -> format_response, with the engine
+    metrics under result["engine"] and total_ms added last; system_one is
+    predict and warmup returns the metrics alone (engine.py:216-229 of the
+    reference).  The Laya SDK and the reference protocol are faked: prepare()
+    must serialise the state with laya.common.serialize_state, tokenise with
+    the engine's tokenizer and config, and truncate left for list states."""
+    import sys
+    import types
+    from laya_b200 import engine as engine_module
+
+    calls = []
+    common = types.ModuleType("laya.common")
+    common.serialize_state = lambda state: ("serialized", tuple(state) if isinstance(state, list) else state)
+    sdk = types.ModuleType("laya")
+    sdk.common = common
+    monkeypatch.setitem(sys.modules, "laya", sdk)
+    monkeypatch.setitem(sys.modules, "laya.common", common)
+
+    def fake_prepare(tok, cfg, state, questions, **kwargs):
+        calls.append(("prepare", tok, dict(cfg), state, len(questions), kwargs))
+        items = [{"ids": [7] * (20 + 10 * i), "markers": [1, 2, 3][: 2 + i % 2], "qtype": i % 3}
+                 for i in range(len(questions))]
+        return PreparedRequest([q["id"] for q in questions], list(questions), items,
+                               sum(len(it["ids"]) for it in items))
+
+    def fake_format(prepared, logits, act, temperature, temperature_by_options):
+        calls.append(("format", logits.shape, act.shape, temperature, dict(temperature_by_options)))
+        return {"answers": {qid: int(np.argmax(logits[i])) for i, qid in enumerate(prepared.ids)}}
+
+    monkeypatch.setattr(engine_module, "prepare_request", fake_prepare)
+    monkeypatch.setattr(engine_module, "format_response", fake_format)
+    engine = make_engine(max_questions=4)
+    engine.tokenizer = "tok"
+    engine.temperature, engine.temperature_by_options = 1.5, {2: 0.5}
+    questions = [{"id": "q0"}, {"id": "q1"}, {"id": "q2"}]
+
+    result = engine.predict(["a", "b"], questions)
+    assert set(result) == {"answers", "engine"}
+    assert set(result["answers"]) == {"q0", "q1", "q2"}
+    metrics = result["engine"]
+    assert {"graph_miss", "graph_build_ms", "shape", "backend", "total_ms"} <= set(metrics)
+    assert metrics["graph_miss"] is True and metrics["shape"] == [4, 64, 4]
+    assert metrics["backend"] == "b200-bf16" and metrics["total_ms"] >= 0.0
+    assert list(metrics)[-1] == "total_ms"
+    kind, tok, cfg, state, count, kwargs = calls[0]
+    assert (kind, tok, cfg, count) == ("prepare", "tok", {"max_len": 512}, 3)
+    assert state == ("serialized", ("a", "b"))
+    assert kwargs == {"max_questions": 4, "truncate_left": True}
+    assert calls[1] == ("format", (3, 4), (3, 2), 1.5, {2: 0.5})
+
+    # system_one is predict; the same shape now hits the captured graph
+    again = engine.system_one({"k": 1}, questions)
+    assert again["engine"]["graph_miss"] is False and again["engine"]["graph_build_ms"] == 0.0
+    assert calls[2][3] == ("serialized", {"k": 1}) and calls[2][5]["truncate_left"] is False
+
+    # warmup returns the metrics dictionary only, total_ms included
+    warm = engine.warmup({"k": 1}, questions[:1])
+    assert set(warm) >= {"graph_miss", "shape", "total_ms"} and warm["shape"] == [1, 64, 2]
+    assert engine.native.captured == [(4, 64, 4, False), (1, 64, 2, False)]
+
+
+def test_prepare_without_tokenizer_names_what_is_missing():
+    engine = make_engine()
+    engine.tokenizer = None
+    with pytest.raises(RuntimeError, match="tokenizer"):
+        engine.predict({}, [{"id": "q"}])
