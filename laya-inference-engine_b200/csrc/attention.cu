@@ -1,349 +1,423 @@
-// Fused RoPE attention for the encoder (global and radius-64 local layers)
-// and the head's key-padded attention.  Replaces rope_qkv + SDPA
-// (src/laya_blackwell/model.py:92-96 and :62-67, kernels.py:62-93).
+// Fused attention for the encoder (global and radius-64 local layers) and the
+// head's key-padded attention, on tcgen05 tensor cores.  Replaces SDPA in
+// src/laya_blackwell/model.py:92-96 (encoder) and :62-67 (head), whose fast
+// paths are the reference's FA2 kernel (fast/native/global_attention.cu:12-68)
+// and its window attention (fast/padded_rope.py:45-92).  q and k arrive
+// rotated: the QKV projection's epilogue applies the rotary embedding.
 //
-// One CTA = 64 queries of one (sequence, head); 4 warps x 16 queries, tensor
-// cores through mma.sync m16n8k16 (bf16, fp32 accumulate).  Local layers only
-// visit key tiles inside [q-64, q+64] (compute skipping, not just masking).
-// Scores and the online softmax are fp32; P is rounded to bf16 for the P.V
-// product (as FlashAttention does); a query that sees no key returns zeros
-// (SDPA's result for a fully masked row).
+// One CTA = 128 queries (the 128 TMEM lanes) of one (sequence, head) against
+// every key those queries can see: all keys of the sequence on global layers,
+// keys [q0 - 64, q0 + 127 + 64] on local layers.  The span is at most 512
+// keys, so the whole score row of a query fits in TMEM (512 fp32 columns) and
+// the softmax is exact and two-pass, with no running-max rescaling of O:
 //
-// Two load paths:
-//  * attention_kernel: Q and K are rotated while they are staged (batch-1
-//    shapes, where the QKV projection's split-K epilogue does not rotate):
-//    y = bf16(fl(a*cos) + fl(b*sin)) in fp32 without FMA contraction.
-//  * attention_async_kernel: the QKV projection already rotated q and k in its
-//    epilogue, so Q, K, V and the key-validity words are copied with cp.async
-//    (zero-filled past the sequence), the next key tile's copies in flight while
-//    the current tile is computed.
-//  * attention_split_kernel: the same copies with eight warps, for grids of
-//    fewer CTAs than SMs: warps 0-3 take the even key tiles and warps 4-7 the
-//    odd ones, each group with its own online softmax, merged at the end; the
-//    next pair of tiles is copied while the current pair is computed.
+//  * warp 0, lane 0: TMA loads of Q (128 rows), every K and V chunk of 64
+//    keys (the [batch][seq][3*hidden] map reads rows past the sequence as
+//    zeros), then the MMAs: S = Q K^T per 128 keys (M=128, N=128, K=64) into
+//    TMEM columns [0, keys), and for each 64-key chunk O += P V (M=128, N=64,
+//    K=64; V is the MN-major B operand straight from its TMA tile) into TMEM
+//    columns [0, 64), which chunk 0's scores free before its P is released.
+//  * warp 1: key-validity bits (one word per 32 keys) and, for the head's
+//    selected query rows, the gather of Q into the swizzled layout.
+//  * warps 2-9: two threads per query row (warps 2-5 and 6-9 cover the four
+//    TMEM lane quarters twice), each owning 32 of every 64 key columns.
+//    Pass 1 reads the row's scores from TMEM and takes the max over visible
+//    keys; pass 2 reads them again, computes p = 2^(s*log2(e)/8 - max), sums
+//    p in fp32 and writes it as two bf16 tiles, hi = bf16(p) and
+//    lo = bf16(p - hi) (128-byte swizzle, double-buffered, in the Q and K
+//    space the score MMAs have finished with); the two halves' max and sum
+//    meet in shared memory; the epilogue scales O by 1/sum and each thread
+//    stores 32 of the row's 64 bf16 outputs.  A warp whose 32 rows all lie
+//    past the last query keeps only the barrier protocol.
+//
+// Numerics: scores and the softmax in fp32; P.V as hi.V + lo.V, which carries
+// p to about 16 significant bits (V is bf16, so each product is exact in the
+// fp32 accumulator) instead of rounding it to bf16 as FlashAttention does:
+// the result tracks an fp32-probability softmax (the reference's CPU path,
+// which its golden outputs come from) to within fp32 summation order.  A query
+// that sees no key returns zeros (SDPA's result for a fully masked row).
+//
+// Every mbarrier wait is bounded; on expiry the CTA records
+// kStatusAttnTimeout, waits (bounded) for its own copies and MMAs, frees TMEM
+// and returns.  TMEM is allocated after griddepcontrol.wait (so the
+// projection before it has released its columns) and the next kernel is
+// released only after the allocation (so it cannot take columns first and
+// then wait on this grid).
 #include "common.cuh"
 #include "params.h"
 #include "launch.h"
-#include "attention_tile.cuh"
 
 #include <mutex>
 
 namespace laya {
 
 namespace {
-using namespace attn;
 
-// Normalise and store this warp's 16 output rows.
-DEVI void store_rows(const Acc& acc, const AttnParams& p, int b, int q0, int h, int warp, int lane) {
-  const int g = lane >> 2, t4 = lane & 3;
-#pragma unroll
-  for (int r = 0; r < 2; ++r) {
-    float l = acc.lrow[r];
-    l += __shfl_xor_sync(0xffffffffu, l, 1);
-    l += __shfl_xor_sync(0xffffffffu, l, 2);
-    const float inv = l > 0.f ? 1.f / l : 0.f;
-    const int qi = q0 + warp * 16 + g + 8 * r;
-    if (qi < p.nq) {
-      __nv_bfloat16* dst = p.out + ((size_t)b * p.nq + qi) * p.ld_out + h * 64;
-#pragma unroll
-      for (int nt = 0; nt < 8; ++nt)
-        *reinterpret_cast<uint32_t*>(dst + nt * 8 + 2 * t4) =
-            pack_bf16(acc.o[nt][2 * r] * inv, acc.o[nt][2 * r + 1] * inv);
-    }
-  }
+constexpr int kTq = 128;          // queries per CTA (TMEM lanes)
+constexpr int kKc = 64;           // keys per chunk (one TMA box, one P tile)
+constexpr int kMaxChunks = 8;     // 512 keys: the TMEM columns of one score row
+constexpr int kThreads = 320;     // warp 0 TMA + MMA, warp 1 setup, warps 2-9 softmax
+constexpr int kSoftmaxThreads = 256;
+constexpr uint32_t kQBytes = kTq * 128;
+constexpr uint32_t kChunkBytes = kKc * 128;
+constexpr uint32_t kPBytes = kTq * 128;
+constexpr float kScaleLog2 = 0.125f * 1.4426950408889634f;  // 1/sqrt(64) * log2(e)
+// O += P V: bf16 x bf16 -> fp32, M = 128, N = 64, B (V) MN-major.
+constexpr uint32_t kIdescPV = idesc_bf16(128, 64) | (1u << 16);
+
+// Shared memory (from a 1024-aligned base): Q, the K region, the V chunks,
+// then barriers, key bits, the TMEM slot and the half-row reductions.  Once
+// every score MMA has completed, Q and the K region hold the four P tiles
+// (hi and lo, two buffers), hence a K region of at least 6 chunks.
+struct Layout {
+  uint32_t k, v, bars, total;
+};
+__host__ __device__ constexpr uint32_t kregion(int chunks) { return (chunks > 6 ? chunks : 6) * kChunkBytes; }
+__host__ __device__ constexpr Layout layout(int chunks) {
+  return Layout{kQBytes, kQBytes + kregion(chunks), kQBytes + kregion(chunks) + chunks * kChunkBytes,
+                kQBytes + kregion(chunks) + chunks * kChunkBytes + 4096};
 }
+struct Bars {
+  uint64_t q, k[kMaxChunks], v[kMaxChunks], s[kMaxChunks / 2], p[2], pv[2], o;
+  uint32_t key_bits[2 * kMaxChunks];
+  uint32_t tmem_slot, failed;
+  float red_max[2][kTq], red_sum[2][kTq];  // the two half-rows' max and sum
+};
+static_assert(sizeof(Bars) <= 4096, "barrier block");
 
-// Key range of the CTA's query tile: all keys, or the tiles covering
-// [q0 - window, q_last + window] on local layers.
-DEVI void key_range(const AttnParams& p, int q0, int& kbeg, int& kend) {
+// Keys [kbeg, kend) that the CTA's queries q0 .. q0+127 can see.
+__host__ __device__ inline void key_span(const AttnParams& p, int q0, int& kbeg, int& kend) {
   kbeg = 0;
   kend = p.s;
-  if (p.window >= 0) {  // queries of this tile are positions q0 .. q0+63
-    const int qmax = min(q0 + AQ, p.nq) - 1;
-    kbeg = max(0, q0 - p.window);
-    kend = min(p.s, qmax + p.window + 1);
-    kbeg = (kbeg / AK) * AK;
+  if (p.window >= 0) {
+    const int qmax = (q0 + kTq < p.nq ? q0 + kTq : p.nq) - 1;
+    kbeg = q0 - p.window > 0 ? q0 - p.window : 0;
+    kend = qmax + p.window + 1 < p.s ? qmax + p.window + 1 : p.s;
   }
 }
+
+DEVI uint32_t pack2(float lo, float hi) {
+  __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&v);
+}
+
+// Named barrier of the softmax warps.
+DEVI void softmax_sync() { asm volatile("bar.sync 1, %0;" ::"n"(kSoftmaxThreads) : "memory"); }
+
+// Keys base .. base+31 (relative to kbeg) that a row seeing keys [lo, hi]
+// sees: the key-validity bits restricted to that range.
+DEVI uint32_t visible_mask(uint32_t bits, int base, int lo, int hi) {
+  const int a = lo - base, z = hi - base;
+  if (a > 31 || z < 0 || a > z) return 0u;
+  const uint32_t from = a <= 0 ? 0xffffffffu : 0xffffffffu << a;
+  const uint32_t to = z >= 31 ? 0xffffffffu : 0xffffffffu >> (31 - z);
+  return bits & from & to;
+}
+
+// 2^x on the SFU (flushes results below 2^-126 to zero; 2^-inf = 0).
+DEVI float ex2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// Max over the visible scores of 32 consecutive keys.
+DEVI float masked_max(const uint32_t (&r)[32], uint32_t vis, float m) {
+  if (vis == 0xffffffffu) {
+#pragma unroll
+    for (int e = 0; e < 32; ++e) m = fmaxf(m, __uint_as_float(r[e]));
+    return m;
+  }
+#pragma unroll
+  for (int e = 0; e < 32; ++e) m = fmaxf(m, (vis >> e) & 1u ? __uint_as_float(r[e]) : -INFINITY);
+  return m;
+}
+
+// bf16 pairs of (a, b) and of their remainders (a - bf16(a), b - bf16(b)).
+DEVI void split2(float a, float b, uint32_t& hi, uint32_t& lo) {
+  const __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+  hi = *reinterpret_cast<const uint32_t*>(&h);
+  lo = pack2(a - __low2float(h), b - __high2float(h));
+}
+
+// p = 2^(s * scale - ms) for visible keys, 0 otherwise; adds p to l and packs
+// the bf16 pairs of p into ph[0..15] and of its remainder into pl.
+DEVI void probs(const uint32_t (&r)[32], uint32_t vis, float ms, float& l, uint32_t* ph, uint32_t* pl) {
+  float p[32];
+  if (vis == 0xffffffffu) {
+#pragma unroll
+    for (int e = 0; e < 32; ++e) p[e] = ex2(__uint_as_float(r[e]) * kScaleLog2 - ms);
+  } else {
+#pragma unroll
+    for (int e = 0; e < 32; ++e) p[e] = ex2((vis >> e) & 1u ? __uint_as_float(r[e]) * kScaleLog2 - ms : -INFINITY);
+  }
+#pragma unroll
+  for (int e = 0; e < 32; e += 2) {
+    l += p[e] + p[e + 1];
+    split2(p[e], p[e + 1], ph[e >> 1], pl[e >> 1]);
+  }
+}
+
+// Byte offset of 16-byte chunk j of row r in a 128-byte-swizzled tile.
+DEVI uint32_t sw128_offset(int r, int j) { return (r >> 3) * 1024 + (r & 7) * 128 + ((j ^ (r & 7)) << 4); }
 
 }  // namespace
 
-__global__ void __launch_bounds__(128) attention_kernel(const AttnParams p) {
-  __shared__ __align__(16) __nv_bfloat16 sQ[AQ * LDS];
-  __shared__ __align__(16) __nv_bfloat16 sK[AK * LDS];
-  __shared__ __align__(16) __nv_bfloat16 sV[AK * LDS];
-  __shared__ int s_qpos[AQ];
-  __shared__ int s_kvalid[AK];
+__global__ void __launch_bounds__(kThreads, 2)
+    attention_tc_kernel(const __grid_constant__ CUtensorMap qkv_map, const AttnParams p, int max_chunks) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const Layout L = layout(max_chunks);
+  uint8_t* sQ = smem;
+  uint8_t* sK = smem + L.k;
+  uint8_t* sV = smem + L.v;
+  Bars& B = *reinterpret_cast<Bars*>(smem + L.bars);
 
-  griddep_launch_dependents();
-  const int q0 = blockIdx.x * AQ, h = blockIdx.y, b = blockIdx.z;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int q0 = blockIdx.x * kTq, h = blockIdx.y, b = blockIdx.z;
+  int kbeg, kend;
+  key_span(p, q0, kbeg, kend);
+  const int nk = kend - kbeg;
+  const int chunks = (nk + kKc - 1) / kKc;
+  const int blocks = (chunks + 1) / 2;
+  const uint32_t tcols = chunks <= 1 ? 64 : chunks <= 2 ? 128 : chunks <= 4 ? 256 : 512;
+  const uint64_t limit = wait_limit(p.wait_limit_us);
+
+  if (tid == 0) {
+    mbar_init(&B.q, 1);
+    for (int i = 0; i < kMaxChunks; ++i) {
+      mbar_init(&B.k[i], 1);
+      mbar_init(&B.v[i], 1);
+    }
+    for (int i = 0; i < kMaxChunks / 2; ++i) mbar_init(&B.s[i], 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&B.p[i], kSoftmaxThreads);
+      mbar_init(&B.pv[i], 1);
+    }
+    mbar_init(&B.o, 1);
+    B.failed = 0;
+    fence_mbar_init();
+    prefetch_tensormap(&qkv_map);
+  }
+  __syncthreads();
   griddep_wait();
 
-  if (tid < AQ) {
-    const int qi = q0 + tid;
-    s_qpos[tid] = qi < p.nq ? (p.q_pos ? p.q_pos[b * p.nq + qi] : qi) : -1;
-  }
-  __syncthreads();
-  const size_t seq_base = (size_t)b * p.s;
-  for (int it = tid; it < AQ * 4; it += 128) {
-    const int r = it >> 2, c = (it & 3) * 8;
-    const int pos = s_qpos[r];
-    uint4 lo = make_uint4(0, 0, 0, 0), hi = lo;
-    if (pos >= 0) {
-      const __nv_bfloat16* src = p.qkv + (seq_base + pos) * p.ld_qkv + h * 64;
-      lo = *reinterpret_cast<const uint4*>(src + c);
-      hi = *reinterpret_cast<const uint4*>(src + c + 32);
-      if (p.cos) rope8(lo, hi, p.cos + (size_t)pos * 64, p.sin + (size_t)pos * 64, c);
-    }
-    *reinterpret_cast<uint4*>(&sQ[r * LDS + c]) = lo;
-    *reinterpret_cast<uint4*>(&sQ[r * LDS + c + 32]) = hi;
-  }
-  int kbeg, kend;
-  key_range(p, q0, kbeg, kend);
-  __syncthreads();
-
-  uint32_t qf[4][4];
-  load_q_frags(qf, sQ, warp, lane);
-  const int g = lane >> 2;
-  const int qpos0 = s_qpos[warp * 16 + g], qpos1 = s_qpos[warp * 16 + g + 8];
-  Acc acc;
-  acc_init(acc);
-
-  for (int k0 = kbeg; k0 < kend; k0 += AK) {
-    __syncthreads();
-    for (int it = tid; it < AK * 4; it += 128) {
-      const int r = it >> 2, c = (it & 3) * 8;
-      const int kp = k0 + r;
-      uint4 klo = make_uint4(0, 0, 0, 0), khi = klo, vlo = klo, vhi = klo;
-      if (kp < p.s) {
-        const __nv_bfloat16* row = p.qkv + (seq_base + kp) * p.ld_qkv;
-        const __nv_bfloat16* ks = row + p.d + h * 64;
-        const __nv_bfloat16* vs = row + 2 * p.d + h * 64;
-        klo = *reinterpret_cast<const uint4*>(ks + c);
-        khi = *reinterpret_cast<const uint4*>(ks + c + 32);
-        vlo = *reinterpret_cast<const uint4*>(vs + c);
-        vhi = *reinterpret_cast<const uint4*>(vs + c + 32);
-        if (p.cos) rope8(klo, khi, p.cos + (size_t)kp * 64, p.sin + (size_t)kp * 64, c);
+  if (warp == 0) {
+    if (lane == 0) {
+      const uint64_t pol = policy_evict_first();
+      if (!p.q_pos) {
+        mbar_expect_tx(&B.q, kQBytes);
+        tma_load_3d(sQ, &qkv_map, &B.q, h * 64, q0, b, pol);
+        tma_load_3d(sQ + kQBytes / 2, &qkv_map, &B.q, h * 64, q0 + 64, b, pol);
       }
-      *reinterpret_cast<uint4*>(&sK[r * LDS + c]) = klo;
-      *reinterpret_cast<uint4*>(&sK[r * LDS + c + 32]) = khi;
-      *reinterpret_cast<uint4*>(&sV[r * LDS + c]) = vlo;
-      *reinterpret_cast<uint4*>(&sV[r * LDS + c + 32]) = vhi;
+      for (int c = 0; c < chunks; ++c) {
+        mbar_expect_tx(&B.k[c], kChunkBytes);
+        tma_load_3d(sK + c * kChunkBytes, &qkv_map, &B.k[c], p.d + h * 64, kbeg + c * kKc, b, pol);
+      }
+      for (int c = 0; c < chunks; ++c) {
+        mbar_expect_tx(&B.v[c], kChunkBytes);
+        tma_load_3d(sV + c * kChunkBytes, &qkv_map, &B.v[c], 2 * p.d + h * 64, kbeg + c * kKc, b, pol);
+      }
     }
-    if (tid < AK) s_kvalid[tid] = (k0 + tid < p.s) ? (p.key_valid[seq_base + k0 + tid] != 0) : 0;
-    __syncthreads();
-    attend_tile(acc, qf, sK, sV, s_kvalid, k0, p.window, qpos0, qpos1, lane);
+    __syncwarp();
+    tmem_alloc(&B.tmem_slot, tcols);
+    tmem_relinquish();
+  } else if (warp == 1) {
+    // all loads first (one latency, not one per word), then the ballots
+    int valid[2 * kMaxChunks];
+    const int* kv = p.key_valid + (size_t)b * p.s + kbeg + lane;
+#pragma unroll
+    for (int w = 0; w < 2 * kMaxChunks; ++w) valid[w] = kbeg + 32 * w + lane < kend ? kv[32 * w] : 0;
+#pragma unroll
+    for (int w = 0; w < 2 * kMaxChunks; ++w) {
+      const uint32_t bits = __ballot_sync(0xffffffffu, valid[w] != 0);
+      if (lane == 0 && w < 2 * chunks) B.key_bits[w] = bits;
+    }
+    if (p.q_pos) {  // selected query rows (head layer): gather Q, zeros past nq
+      for (int it = lane; it < kTq * 8; it += 32) {
+        const int r = it >> 3, j = it & 7, qi = q0 + r;
+        uint4 v = make_uint4(0, 0, 0, 0);
+        if (qi < p.nq) {
+          const int pos = p.q_pos[b * p.nq + qi];
+          v = *reinterpret_cast<const uint4*>(p.qkv + ((size_t)b * p.s + pos) * p.ld_qkv + h * 64 + j * 8);
+        }
+        *reinterpret_cast<uint4*>(sQ + sw128_offset(r, j)) = v;
+      }
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&B.q);
+    }
   }
-  store_rows(acc, p, b, q0, h, warp, lane);
-}
-
-__global__ void __launch_bounds__(128) attention_async_kernel(const AttnParams p) {
-  __shared__ __align__(16) __nv_bfloat16 sQ[AQ * LDS];
-  __shared__ __align__(16) __nv_bfloat16 sK[2][AK * LDS];
-  __shared__ __align__(16) __nv_bfloat16 sV[2][AK * LDS];
-  __shared__ __align__(16) int s_kvalid[2][AK];
-  __shared__ int s_qpos[AQ];
-
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
   griddep_launch_dependents();
-  const int q0 = blockIdx.x * AQ, h = blockIdx.y, b = blockIdx.z;
-  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  griddep_wait();
+  const uint32_t tmem = B.tmem_slot;
 
-  if (tid < AQ) {
-    const int qi = q0 + tid;
-    s_qpos[tid] = qi < p.nq ? (p.q_pos ? p.q_pos[b * p.nq + qi] : qi) : -1;
-  }
-  __syncthreads();
-  const size_t seq_base = (size_t)b * p.s;
-  // Q: 64 rows x 8 chunks of 16 bytes
-  for (int it = tid; it < AQ * 8; it += 128) {
-    const int r = it >> 3, c = (it & 7) * 8;
-    const int pos = s_qpos[r];
-    const __nv_bfloat16* src = pos >= 0 ? p.qkv + (seq_base + pos) * p.ld_qkv + h * 64 + c : p.qkv;
-    cp_async16(&sQ[r * LDS + c], src, pos >= 0);
-  }
-  int kbeg, kend;
-  key_range(p, q0, kbeg, kend);
-  const int ntiles = (kend - kbeg + AK - 1) / AK;
-  auto issue_tile = [&](int t) {
-    const int k0 = kbeg + t * AK, buf = t & 1;
-    for (int it = tid; it < AK * 8; it += 128) {
-      const int r = it >> 3, c = (it & 7) * 8;
-      const int kp = k0 + r;
-      const bool ok = kp < p.s;
-      const __nv_bfloat16* row = ok ? p.qkv + (seq_base + kp) * p.ld_qkv : p.qkv;
-      cp_async16(&sK[buf][r * LDS + c], row + p.d + h * 64 + c, ok);
-      cp_async16(&sV[buf][r * LDS + c], row + 2 * p.d + h * 64 + c, ok);
+  if (tid == 0) {
+    // ---- MMA issue: scores for every 128 keys, then O += P V per chunk
+    bool ok = mbar_wait(&B.q, 0, limit);
+    const uint64_t qd = sw128_desc(smem_u32(sQ));
+    for (int j = 0; ok && j < blocks; ++j) {
+      ok = mbar_wait(&B.k[2 * j], 0, limit) && (2 * j + 1 >= chunks || mbar_wait(&B.k[2 * j + 1], 0, limit));
+      if (!ok) break;
+      tc_fence_after();
+      const uint32_t idesc = idesc_bf16(128, 2 * j + 1 < chunks ? 128 : 64);
+      const uint64_t kd = sw128_desc(smem_u32(sK + 2 * j * kChunkBytes));
+#pragma unroll
+      for (int kk = 0; kk < 4; ++kk) umma_f16(tmem + j * 128, qd + 2 * kk, kd + 2 * kk, idesc, kk != 0);
+      umma_commit(&B.s[j]);
     }
-    if (tid < AK) {
-      const bool ok = k0 + tid < p.s;
-      cp_async4(&s_kvalid[buf][tid], ok ? p.key_valid + seq_base + k0 + tid : p.key_valid, ok);
-    }
-    cp_commit();
-  };
-  if (ntiles > 0) issue_tile(0);  // first group also carries Q
-  else cp_commit();
-
-  const int g = lane >> 2;
-  const int qpos0 = s_qpos[warp * 16 + g], qpos1 = s_qpos[warp * 16 + g + 8];
-  Acc acc;
-  acc_init(acc);
-  uint32_t qf[4][4];
-  for (int t = 0; t < ntiles; ++t) {
-    if (t + 1 < ntiles) {
-      issue_tile(t + 1);
-      cp_wait_all_but_one();
-    } else {
-      cp_wait_all();
-    }
-    __syncthreads();
-    if (t == 0) load_q_frags(qf, sQ, warp, lane);
-    attend_tile(acc, qf, sK[t & 1], sV[t & 1], s_kvalid[t & 1], kbeg + t * AK, p.window, qpos0, qpos1, lane);
-    __syncthreads();  // buffer t & 1 is refilled by the copies issued in the next iteration
-  }
-  cp_wait_all();
-  store_rows(acc, p, b, q0, h, warp, lane);
-}
-
-// Shared memory of attention_split_kernel: Q, two stages x two key groups of
-// K and V tiles, their key-validity words, the query positions.
-constexpr int kSplitThreads = 256;
-constexpr int kTileBytes = AK * LDS * 2;
-constexpr int kSplitSmem = AQ * LDS * 2 + 8 * kTileBytes + 4 * AK * 4 + AQ * 4;
-
-__global__ void __launch_bounds__(kSplitThreads) attention_split_kernel(const AttnParams p) {
-  extern __shared__ __align__(16) uint8_t att_smem[];
-  __nv_bfloat16* sQ = reinterpret_cast<__nv_bfloat16*>(att_smem);
-  // K tile of (stage st, group gr) at sKV + (st * 2 + gr) * 2 tiles, V right after it
-  __nv_bfloat16* sKV = sQ + AQ * LDS;
-  int* s_kvalid = reinterpret_cast<int*>(att_smem + AQ * LDS * 2 + 8 * kTileBytes);  // [stage][group][AK]
-  int* s_qpos = s_kvalid + 4 * AK;
-
-  griddep_launch_dependents();
-  const int q0 = blockIdx.x * AQ, h = blockIdx.y, b = blockIdx.z;
-  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int grp = warp >> 2, qw = warp & 3;  // key group, query quarter
-  griddep_wait();
-
-  if (tid < AQ) {
-    const int qi = q0 + tid;
-    s_qpos[tid] = qi < p.nq ? (p.q_pos ? p.q_pos[b * p.nq + qi] : qi) : -1;
-  }
-  __syncthreads();
-  const size_t seq_base = (size_t)b * p.s;
-  // Q: 64 rows x 8 chunks of 16 bytes
-  for (int it = tid; it < AQ * 8; it += kSplitThreads) {
-    const int r = it >> 3, c = (it & 7) * 8;
-    const int pos = s_qpos[r];
-    const __nv_bfloat16* src = pos >= 0 ? p.qkv + (seq_base + pos) * p.ld_qkv + h * 64 + c : p.qkv;
-    cp_async16(&sQ[r * LDS + c], src, pos >= 0);
-  }
-  int kbeg, kend;
-  key_range(p, q0, kbeg, kend);
-  const int ntiles = (kend - kbeg + AK - 1) / AK;
-  const int npairs = (ntiles + 1) / 2;
-  // step j: key tile 2j for group 0, 2j+1 for group 1, into stage j & 1
-  auto issue_pair = [&](int j) {
-    const int st = j & 1;
-    for (int it = tid; it < 2 * AK * 8; it += kSplitThreads) {
-      const int gr = it / (AK * 8), r = (it >> 3) & (AK - 1), c = (it & 7) * 8;
-      const int t = 2 * j + gr;
-      if (t >= ntiles) continue;
-      const int kp = kbeg + t * AK + r;
-      const bool ok = kp < p.s;
-      const __nv_bfloat16* row = ok ? p.qkv + (seq_base + kp) * p.ld_qkv : p.qkv;
-      __nv_bfloat16* sK = sKV + (st * 2 + gr) * 2 * AK * LDS;
-      cp_async16(&sK[r * LDS + c], row + p.d + h * 64 + c, ok);
-      cp_async16(&sK[AK * LDS + r * LDS + c], row + 2 * p.d + h * 64 + c, ok);
-    }
-    if (tid < 2 * AK) {
-      const int gr = tid / AK, t = 2 * j + gr, kp = kbeg + t * AK + (tid & (AK - 1));
-      if (t < ntiles) {
-        const bool ok = kp < p.s;
-        cp_async4(&s_kvalid[(st * 2 + gr) * AK + (tid & (AK - 1))], ok ? p.key_valid + seq_base + kp : p.key_valid, ok);
+    for (int c = 0; ok && c < chunks; ++c) {
+      ok = mbar_wait(&B.p[c & 1], (c >> 1) & 1, limit) && mbar_wait(&B.v[c], 0, limit);
+      if (!ok) break;
+      tc_fence_after();
+      const uint64_t hd = sw128_desc(smem_u32(sQ + (c & 1) * 2 * kPBytes));
+      const uint64_t ld = sw128_desc(smem_u32(sQ + ((c & 1) * 2 + 1) * kPBytes));
+      const uint64_t vd = sw128_desc(smem_u32(sV + c * kChunkBytes));
+      // K steps of 16: 32 bytes along P's rows, 16 rows (2048 bytes) down V
+#pragma unroll
+      for (int kk = 0; kk < 4; ++kk) {
+        umma_f16(tmem, hd + 2 * kk, vd + 128 * kk, kIdescPV, (c | kk) != 0);
+        umma_f16(tmem, ld + 2 * kk, vd + 128 * kk, kIdescPV, 1);
       }
+      umma_commit(&B.pv[c & 1]);
     }
-    cp_commit();
-  };
-  if (npairs > 0) issue_pair(0);  // first group also carries Q
-  else cp_commit();
-
-  const int g = lane >> 2;
-  const int qpos0 = s_qpos[qw * 16 + g], qpos1 = s_qpos[qw * 16 + g + 8];
-  Acc acc;
-  acc_init(acc);
-  uint32_t qf[4][4];
-  for (int j = 0; j < npairs; ++j) {
-    if (j + 1 < npairs) {
-      issue_pair(j + 1);
-      cp_wait_all_but_one();
-    } else {
-      cp_wait_all();
+    if (!ok) {
+      record_status(p.status, kStatusAttnTimeout);
+      atomicExch(&B.failed, 1u);
     }
-    __syncthreads();
-    if (j == 0) load_q_frags(qf, sQ, qw, lane);
-    const int t = 2 * j + grp, st = j & 1;
-    if (t < ntiles) {
-      const __nv_bfloat16* sK = sKV + (st * 2 + grp) * 2 * AK * LDS;
-      attend_tile(acc, qf, sK, sK + AK * LDS, s_kvalid + (st * 2 + grp) * AK, kbeg + t * AK, p.window, qpos0, qpos1,
-                  lane);
+    umma_commit(&B.o);
+  } else if (warp >= 2) {
+    // ---- softmax: two threads per query row (TMEM lane = row), thread `half`
+    // owning columns [32 * half, 32 * half + 32) of every 64-key chunk
+    const int quarter = warp & 3, half = (warp - 2) >> 2;
+    const int row = quarter * 32 + lane, qi = q0 + row;
+    int qp = -1;
+    if (qi < p.nq) qp = p.q_pos ? p.q_pos[b * p.nq + qi] : qi;
+    int lo = 0, hi = nk - 1;  // visible keys relative to kbeg
+    if (qp < 0) {
+      lo = 1;
+      hi = 0;
+    } else if (p.window >= 0) {
+      lo = max(lo, qp - p.window - kbeg);
+      hi = min(hi, qp + p.window - kbeg);
     }
-    __syncthreads();  // stage j & 1 is refilled by the copies issued in the next step
-  }
-  cp_wait_all();
-  __syncthreads();
-  // merge the two key groups' online-softmax states (same fragment layout):
-  // m = max(m0, m1), l and O rescaled by exp2(m_i - m)
-  float* xch = reinterpret_cast<float*>(sKV) + (qw * 32 + lane) * 36;
-  if (grp == 1) {
-#pragma unroll
-    for (int nt = 0; nt < 8; ++nt)
-#pragma unroll
-      for (int e = 0; e < 4; ++e) xch[nt * 4 + e] = acc.o[nt][e];
-    xch[32] = acc.mrow[0];
-    xch[33] = acc.mrow[1];
-    xch[34] = acc.lrow[0];
-    xch[35] = acc.lrow[1];
-  }
-  __syncthreads();
-  if (grp == 0) {
-#pragma unroll
-    for (int r = 0; r < 2; ++r) {
-      const float m1 = xch[32 + r], l1 = xch[34 + r], m0 = acc.mrow[r];
-      const float m = fmaxf(m0, m1);
-      const float c0 = m == -INFINITY ? 0.f : exp2f(m0 - m);
-      const float c1 = m == -INFINITY ? 0.f : exp2f(m1 - m);
-      acc.lrow[r] = acc.lrow[r] * c0 + l1 * c1;
-#pragma unroll
-      for (int nt = 0; nt < 8; ++nt) {
-        acc.o[nt][2 * r] = acc.o[nt][2 * r] * c0 + xch[nt * 4 + 2 * r] * c1;
-        acc.o[nt][2 * r + 1] = acc.o[nt][2 * r + 1] * c0 + xch[nt * 4 + 2 * r + 1] * c1;
+    const uint32_t taddr = tmem + ((uint32_t)(quarter * 32) << 16) + 32 * half;
+    // a warp whose 32 rows are all past the last query only keeps the barrier
+    // protocol: its rows of P and O are never stored, so they are not computed
+    const bool live = __any_sync(0xffffffffu, qp >= 0);
+    bool ok = true;
+    float m = -INFINITY;
+    for (int j = 0; live && j < blocks; ++j) {
+      ok = __all_sync(0xffffffffu, mbar_wait(&B.s[j], 0, limit));
+      if (!ok) break;
+      tc_fence_after();
+      const int c0 = 2 * j, base0 = c0 * kKc + 32 * half, base1 = base0 + kKc;
+      uint32_t r0[32], r1[32];
+      tmem_ld32(taddr + c0 * kKc, r0);
+      if (c0 + 1 < chunks) tmem_ld32(taddr + (c0 + 1) * kKc, r1);
+      tmem_wait_ld();
+      m = masked_max(r0, visible_mask(B.key_bits[base0 >> 5], base0, lo, hi), m);
+      if (c0 + 1 < chunks) m = masked_max(r1, visible_mask(B.key_bits[base1 >> 5], base1, lo, hi), m);
+    }
+    B.red_max[half][row] = m;
+    softmax_sync();
+    m = fmaxf(B.red_max[0][row], B.red_max[1][row]);
+    const float ms = m == -INFINITY ? 0.f : m * kScaleLog2;
+    float l = 0.f;
+    for (int c = 0; ok && c < chunks; ++c) {
+      const int buf = c & 1;
+      if (c >= 2) {  // the P.V of chunk c - 2 has released this buffer
+        ok = __all_sync(0xffffffffu, mbar_wait(&B.pv[buf], ((c - 2) >> 1) & 1, limit));
+        if (!ok) break;
+        tc_fence_after();
       }
-      acc.mrow[r] = m;
+      if (live) {
+        const int base = c * kKc + 32 * half;
+        uint32_t r[32], ph[16], pl[16];
+        tmem_ld32(taddr + c * kKc, r);
+        tmem_wait_ld();
+        probs(r, visible_mask(B.key_bits[base >> 5], base, lo, hi), ms, l, ph, pl);
+        uint8_t* tile = sQ + buf * 2 * kPBytes;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const uint32_t off = sw128_offset(row, 4 * half + j);
+          *reinterpret_cast<uint4*>(tile + off) = make_uint4(ph[4 * j], ph[4 * j + 1], ph[4 * j + 2], ph[4 * j + 3]);
+          *reinterpret_cast<uint4*>(tile + kPBytes + off) =
+              make_uint4(pl[4 * j], pl[4 * j + 1], pl[4 * j + 2], pl[4 * j + 3]);
+        }
+        fence_proxy_async_smem();
+      }
+      tc_fence_before();
+      mbar_arrive(&B.p[buf]);
     }
-    store_rows(acc, p, b, q0, h, qw, lane);
+    B.red_sum[half][row] = l;
+    softmax_sync();
+    l = B.red_sum[0][row] + B.red_sum[1][row];
+    if (ok) ok = __all_sync(0xffffffffu, mbar_wait(&B.o, 0, limit));
+    if (ok && live) {
+      tc_fence_after();
+      uint32_t r[32];
+      tmem_ld32(taddr, r);
+      tmem_wait_ld();
+      if (qi < p.nq) {
+        const float inv = l > 0.f ? 1.f / l : 0.f;
+        uint4* dst = reinterpret_cast<uint4*>(p.out + ((size_t)b * p.nq + qi) * p.ld_out + h * 64 + 32 * half);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const uint32_t* x = r + 8 * j;
+          dst[j] = make_uint4(pack2(__uint_as_float(x[0]) * inv, __uint_as_float(x[1]) * inv),
+                              pack2(__uint_as_float(x[2]) * inv, __uint_as_float(x[3]) * inv),
+                              pack2(__uint_as_float(x[4]) * inv, __uint_as_float(x[5]) * inv),
+                              pack2(__uint_as_float(x[6]) * inv, __uint_as_float(x[7]) * inv));
+        }
+      }
+    } else if (!ok) {
+      record_status(p.status, kStatusAttnTimeout);
+      atomicExch(&B.failed, 1u);
+    }
+  }
+
+  // ---- teardown: after a failure, wait (bounded) for this CTA's copies and
+  // MMAs before its shared memory and TMEM are released
+  __syncthreads();
+  if (tid == 0 && B.failed) {
+    if (!p.q_pos) mbar_wait(&B.q, 0, limit);
+    for (int c = 0; c < chunks; ++c) {
+      mbar_wait(&B.k[c], 0, limit);
+      mbar_wait(&B.v[c], 0, limit);
+    }
+    mbar_wait(&B.o, 0, limit);
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    tc_fence_after();
+    tmem_dealloc(tmem, tcols);
   }
 }
 
-cudaError_t launch_attention(const AttnParams& p, int batch, int heads, cudaStream_t stream, bool pdl) {
-  if (p.window >= 0 && p.q_pos) return cudaErrorInvalidValue;
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3((p.nq + AQ - 1) / AQ, heads, batch);
-  cfg.blockDim = dim3(128, 1, 1);
-  cfg.stream = stream;
-  cudaLaunchAttribute attr;
-  attr.id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr.val.programmaticStreamSerializationAllowed = 1;
-  cfg.attrs = &attr;
-  cfg.numAttrs = pdl ? 1 : 0;
-  if (p.cos) return cudaLaunchKernelEx(&cfg, attention_kernel, p);
-  // Fewer CTAs than SMs (long sequences at small batch): split the key tiles
-  // over two warp groups (measured 2.07 -> 1.85 ms per C3 forward); with
-  // several CTAs per SM the four-warp kernel is faster (C2: 2.62 vs 2.75 ms).
+// ------------------------------------------------------------------ host side
+
+int attention_chunks(const AttnParams& p) {
+  int most = 0;
+  for (int q0 = 0; q0 < p.nq; q0 += kTq) {
+    int kbeg, kend;
+    key_span(p, q0, kbeg, kend);
+    const int c = (kend - kbeg + kKc - 1) / kKc;
+    most = c > most ? c : most;
+  }
+  return most;
+}
+
+cudaError_t launch_attention(const AttnParams& p, const CUtensorMap& qkv_map, int batch, int heads,
+                             cudaStream_t stream, bool pdl) {
+  if ((p.window >= 0 && p.q_pos) || p.nq < 1 || p.s < 1 || batch < 1 || heads < 1) return cudaErrorInvalidValue;
+  const int chunks = attention_chunks(p);
+  if (chunks < 1 || chunks > kMaxChunks) return cudaErrorInvalidValue;
   static std::mutex mu;
   static uint64_t ready = 0;
-  static int sms[64] = {0};
   int dev = 0;
   cudaError_t err = cudaGetDevice(&dev);
   if (err != cudaSuccess) return err;
@@ -351,17 +425,28 @@ cudaError_t launch_attention(const AttnParams& p, int batch, int heads, cudaStre
   {
     std::lock_guard<std::mutex> lock(mu);
     if (!(ready >> dev & 1)) {
-      err = cudaFuncSetAttribute(attention_split_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSplitSmem);
-      if (err == cudaSuccess) err = cudaDeviceGetAttribute(&sms[dev], cudaDevAttrMultiProcessorCount, dev);
+      err = cudaFuncSetAttribute(attention_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int)layout(kMaxChunks).total + 1024);
+      // all of the unified L1 / shared storage as shared memory, so that two
+      // CTAs of up to four chunks each fit on one SM
+      if (err == cudaSuccess)
+        err = cudaFuncSetAttribute(attention_tc_kernel, cudaFuncAttributePreferredSharedMemoryCarveout,
+                                   (int)cudaSharedmemCarveoutMaxShared);
       if (err != cudaSuccess) return err;
       ready |= uint64_t(1) << dev;
     }
   }
-  const long long ctas = (long long)cfg.gridDim.x * cfg.gridDim.y * cfg.gridDim.z;
-  if (ctas > sms[dev]) return cudaLaunchKernelEx(&cfg, attention_async_kernel, p);
-  cfg.blockDim = dim3(kSplitThreads, 1, 1);
-  cfg.dynamicSmemBytes = kSplitSmem;
-  return cudaLaunchKernelEx(&cfg, attention_split_kernel, p);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((p.nq + kTq - 1) / kTq, heads, batch);
+  cfg.blockDim = dim3(kThreads, 1, 1);
+  cfg.dynamicSmemBytes = layout(chunks).total + 1024;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr;
+  attr.id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr.val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = &attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, attention_tc_kernel, qkv_map, p, chunks);
 }
 
 }  // namespace laya

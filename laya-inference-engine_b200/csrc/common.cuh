@@ -101,6 +101,16 @@ DEVI void tma_load_2d(void* dst, const CUtensorMap* map, uint64_t* bar, int x, i
       : "memory");
 }
 
+// 3-D tile load ([batch][rows][cols] tensors: rows past a batch entry's end
+// read as zeros instead of the next entry's first rows).
+DEVI void tma_load_3d(void* dst, const CUtensorMap* map, uint64_t* bar, int x, int y, int z, uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint"
+      " [%0], [%1, {%3, %4, %5}], [%2], %6;" ::"r"(smem_u32(dst)),
+      "l"(map), "r"(smem_u32(bar)), "r"(x), "r"(y), "r"(z), "l"(policy)
+      : "memory");
+}
+
 // Tile store from shared memory (rows beyond the tensor's extent are clipped).
 DEVI void tma_store_2d(const CUtensorMap* map, const void* src, int x, int y) {
   asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(map),

@@ -103,6 +103,24 @@ CUtensorMap make_map(const void* ptr, int rows, int cols, int esize, int box_row
   return m;
 }
 
+// [batch][seq][ld] bf16 rows (the QKV projection's output) for the attention
+// kernel: box 64 columns (one head) x 64 rows x 1, 128-byte swizzle; rows past
+// a sequence's end read as zeros.
+CUtensorMap make_seq_map(const void* ptr, int batch, int seq, int ld) {
+  EncodeTiledFn enc = get_encode_fn();
+  if (!enc) fail("cuTensorMapEncodeTiled is unavailable");
+  CUtensorMap m;
+  cuuint64_t dims[3] = {(cuuint64_t)ld, (cuuint64_t)seq, (cuuint64_t)batch};
+  cuuint64_t strides[2] = {(cuuint64_t)ld * 2, (cuuint64_t)seq * ld * 2};
+  cuuint32_t box[3] = {64, 64, 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = enc(&m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(ptr), dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) fail("cuTensorMapEncodeTiled failed (%d) for a %dx%dx%d sequence map", (int)r, batch, seq, ld);
+  return m;
+}
+
 // Plain (unswizzled) 2D map for the TMA epilogue: a [rows][ld] row-major
 // buffer of `esize`-byte elements, box = box_cols x box_rows.  Returns false
 // when the driver rejects the geometry (the caller then uses the register
@@ -321,7 +339,7 @@ void validate_cfg(const laya_b200_config& c) {
   if (c.head_ff % 128 || c.head_ff <= 0) fail("head_ff must be a positive multiple of 128");
   if (c.hidden / c.head_heads != 64 || c.hidden % c.head_heads) fail("head attention needs 64-wide heads");
   if (c.layers < 1 || c.vocab < 1 || c.num_qtypes < 1 || c.head_layers < 0) fail("bad layer / vocab counts");
-  if (c.max_len < 1 || c.max_len > 8192) fail("max_len out of range");
+  if (c.max_len < 1 || c.max_len > 512) fail("max_len must be in [1, 512] (attention keeps a query's scores in TMEM)");
   if (c.global_every < 1 || c.local_window < 0) fail("bad attention pattern");
   if (c.act_hidden < 32 || c.act_hidden > 1024 || c.act_hidden % 32) fail("act_hidden must be a multiple of 32");
   if (c.max_batch < 1 || c.max_options < 2 || c.max_options > 256) fail("max_batch >= 1, 2 <= max_options <= 256");
@@ -422,7 +440,7 @@ struct Fwd {
   // most four heads).  Returns false,
   // launching nothing, when the shape does not qualify.
   bool gemm_attn(const Proj& w, const AttnParams& a, int M) {
-    if (w.kind != kKindBf16 || a.q_pos || a.nq != a.s || a.s != M || M <= 32 || M > 64 || w.K % 64 || a.cos)
+    if (w.kind != kKindBf16 || a.q_pos || a.nq != a.s || a.s != M || M <= 32 || M > 64 || w.K % 64)
       return false;
     const int kb = w.K / 64;
     int bn = 0, split = 1;
@@ -584,9 +602,13 @@ struct Fwd {
     count(launch_norm(p, st, pdl()), "norm launch");
   }
 
-  void attention(const AttnParams& p, int batch, int heads) {
+  void attention(AttnParams p, int batch, int heads) {
     if (!on(kCatAttention)) return;
-    count(launch_attention(p, batch, heads, st, pdl()), "attention launch");
+    const int chunks = attention_chunks(p);
+    if (chunks < 1 || chunks > 8) fail("attention over %d keys: at most 512 per query tile", chunks * 64);
+    p.status = e->status_dev;
+    const CUtensorMap map = make_seq_map(p.qkv, batch, p.s, p.ld_qkv);
+    count(launch_attention(p, map, batch, heads, st, pdl()), "attention launch");
   }
 
   // Token-table rows [v0, v0 + n): the embedding LayerNorm of those ids and
@@ -723,7 +745,8 @@ struct Fwd {
       const bool glob = (i % c.global_every) == 0;
       const float* rc = glob ? E.gcos : E.lcos;
       const float* rs = glob ? E.gsin : E.lsin;
-      // The rotary embedding runs in the projection's epilogue.
+      // The rotary embedding runs in the projection's epilogue (the token
+      // tables hold layer 0's rotated q and k).
       bool rotated = true;
       if (tables && i == 0) {
         // layer-0 qkv came from the token tables
@@ -740,8 +763,7 @@ struct Fwd {
       a.s = s;
       a.nq = s;
       a.key_valid = valid;
-      a.cos = rotated ? nullptr : rc;
-      a.sin = rotated ? nullptr : rs;
+      if (!rotated) fail("layer %d: the QKV projection did not apply the rotary embedding", i);
       a.window = glob ? -1 : c.local_window;
       a.out = E.attn;
       a.ld_out = d;
@@ -1483,6 +1505,7 @@ int laya_b200_read_buffer(laya_b200_engine* e, const char* name, void* dst, size
     else if (n == "attn") { src = e->attn; cap = T * d * 2; }
     else if (n == "g") { src = e->g; cap = T * (size_t)(c.intermediate > c.head_ff ? c.intermediate : c.head_ff) * 2; }
     else if (n == "hsel") { src = e->hsel; cap = R * d * 4; }
+    else if (n == "asel") { src = e->asel; cap = R * d * 2; }
     else if (n == "msc") { src = e->msc; cap = BK * d * 2; }
     else if (n == "zsc") { src = e->zsc; cap = BK * d * 2; }
     else if (n == "n8" && e->n8) { src = e->n8; cap = T * d; }

@@ -169,7 +169,7 @@ __global__ void __launch_bounds__(kFaThreads, 1)
 cudaError_t launch_gemm_attn(const CUtensorMap& wmap, const GemmParams& p, const AttnParams& a, int split,
                              cudaStream_t stream, bool pdl) {
   if (p.N % 128 || p.M <= 32 || p.M > kFaBN || a.s != p.M || split < 1 || split > 16 || split > p.kblocks ||
-      p.kblocks * 64 != p.K || p.K != a.d || p.epilogue != kEpiResidual || a.q_pos || a.nq != a.s || a.cos ||
+      p.kblocks * 64 != p.K || p.K != a.d || p.epilogue != kEpiResidual || a.q_pos || a.nq != a.s ||
       !p.ln_stats || p.bias)
     return cudaErrorInvalidValue;
   if ((p.kblocks + split - 1) / split > kFaStages) return cudaErrorInvalidValue;

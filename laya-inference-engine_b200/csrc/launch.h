@@ -33,7 +33,13 @@ cudaError_t launch_nvfp4_pack_weight(const __nv_bfloat16* w, int rows, int k, un
                                      uint8_t* sf, int col_blocks, float* tensor_scale, cudaStream_t stream);
 cudaError_t launch_quant_nvfp4(const QuantParams& p, int rows_per_block, int col_blocks, cudaStream_t stream,
                                bool pdl);
-cudaError_t launch_attention(const AttnParams& p, int batch, int heads, cudaStream_t stream, bool pdl);
+// Attention of `heads` heads of `batch` sequences on tcgen05 tensor cores;
+// qkv_map: 3-D map of p.qkv as [batch][s][ld_qkv] bf16, box 64 x 64 x 1,
+// 128-byte swizzle.  At most 512 keys visible to any 128-query tile.
+cudaError_t launch_attention(const AttnParams& p, const CUtensorMap& qkv_map, int batch, int heads,
+                             cudaStream_t stream, bool pdl);
+// Chunks of 64 keys the widest query tile of p sees (the kernel takes <= 8).
+int attention_chunks(const AttnParams& p);
 cudaError_t launch_norm(const NormParams& p, cudaStream_t stream, bool pdl);
 cudaError_t launch_quant_fp8(const QuantParams& p, cudaStream_t stream, bool pdl);
 cudaError_t launch_gather_rows(float* dst, const float* src, const int* map, int rows, int d, cudaStream_t stream,

@@ -128,11 +128,11 @@ struct AttnParams {
   int nq;                    // queries per sequence
   const int* q_pos;          // [b][nq] query positions, or null (query i at position i)
   const int* key_valid;      // [b][s] 1 = visible key
-  const float* cos;          // [max_len][64] or null (no rotary)
-  const float* sin;
   int window;                // -1 global; else |q - k| <= window
   __nv_bfloat16* out;        // [b*nq][ld_out]
   int ld_out;
+  uint32_t* status;          // device-visible status word (bounded waits)
+  uint32_t wait_limit_us;    // 0: the default limit
 };
 
 struct QuantParams {

@@ -56,6 +56,8 @@ class LayaConfig:
             raise ValueError("intermediate must be a multiple of 64")
         if self.head_ff % 128:
             raise ValueError("head_ff must be a multiple of 128")
+        if not 1 <= self.max_len <= 512:
+            raise ValueError("max_len must be in [1, 512]: attention keeps a query's scores in tensor memory")
         if self.hidden // self.head_heads != 64:
             raise ValueError("head attention must also use 64-wide heads")
         if self.act_hidden % 32 or self.act_hidden > 1024:

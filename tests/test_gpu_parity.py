@@ -115,15 +115,16 @@ def test_invalid_inputs_are_rejected_on_the_host():
     nf.run(slot, inp)  # the engine stays usable
 
 
-# FP8 at C2: with the reference's own FP8 quantisation (pinned bit-exactly by
-# tests/golden/fp8_linear) the logits miss north_star's 6e-2 bf16 criterion on
-# this case by 5e-4 (measured 0.0605 on a B200; every decision agrees).  The
-# tolerance stays; the miss is recorded rather than hidden.
-_FP8_C2_MISS = pytest.mark.xfail(strict=False, reason="FP8 (reference recipe) vs bf16 at C2 measured 0.0605 > 6e-2")
+# FP8 at C2 is the tightest case: with the reference's own FP8 quantisation
+# (pinned bit-exactly by tests/golden/fp8_linear) the logits sit at 0.0586 of
+# the reference's bf16 golden against north_star's 6e-2 (measured on a B200
+# with the tensor-core attention, whose P.V carries p to about 16 bits; with
+# P rounded to bf16 in an online softmax the same case measured 0.0605).
+# Every decision agrees.
 
 
 @pytest.mark.parametrize("precision,golden", [
-    ("fp8", "laya_c1_noul_full"), pytest.param("fp8", "laya_c2_b16_s96", marks=_FP8_C2_MISS),
+    ("fp8", "laya_c1_noul_full"), ("fp8", "laya_c2_b16_s96"),
     ("nvfp4", "laya_c1_noul_full"), ("nvfp4", "laya_c3_s512_full"),
 ])
 def test_low_precision_meets_the_tolerance_against_the_reference_bf16(precision, golden):
@@ -163,17 +164,46 @@ def test_fp8_matches_fp8_oracle(name, lengths, s, k):
 
 def test_nvfp4_long_question_matches_nvfp4_oracle():
     """NVFP4, one question at the model maximum (s=512):
-    10 global layers and 18 radius-64 local layers."""
+    10 global layers and 18 radius-64 local layers.
+
+    Two NVFP4 forwards whose arithmetic differs only in fp32 summation order
+    land about 0.1 apart: an activation that sits on an e2m1 rounding boundary
+    of its 16-element block goes one way or the other, and 28 layers carry the
+    difference to the logits.  Measured on this input: the NVFP4 oracle is
+    0.112 from the reference's bf16 golden, the GPU 0.098, and the two are
+    0.13 to 0.18 apart depending on the attention kernel's summation order
+    alone.  The NVFP4 arithmetic itself is held bit for bit elsewhere (the
+    quantisers and the QKV stage, test_gpu_kernels.py); here the whole forward
+    must (a) take the NVFP4 oracle's decision wherever the oracle's top-2
+    margin exceeds 0.15, (b) lie within 0.15 of the bf16 oracle, north_star's
+    bound, (c) be no less accurate than the NVFP4 oracle (its distance to the
+    bf16 oracle at most the oracle's own plus 0.05) and (d) lie within 0.3,
+    twice the bound, of the NVFP4 oracle."""
     name, s = "laya", 512
+    tol = TOL["nvfp4"]
     nf = engine_for(name, "nvfp4")
     items = synthetic_items([512], ["choice"], seed=40, vocab=CONFIGS[name].vocab)
     inp = pack(items, 1, s, 4, CONFIGS[name].pad_token_id)
     slot = nf.capture(1, s, 4, True)
     logits, act = nf.run(slot, inp)
+    mm = inp["marker_mask"].astype(bool)
     ol, oa = oracle_for(name, "nvfp4").forward(**inp)
-    compare(logits, act, ol, oa, inp["marker_mask"], TOL["nvfp4"], "nvfp4 C3 vs nvfp4 oracle")
-    bl, _ = oracle_for(name, "bf16").forward(**inp)
-    print(f"nvfp4 decision agreement with the bf16 oracle: {O.decision_agreement(bl, logits, inp['marker_mask']):.3f}")
+    bl, ba = oracle_for(name, "bf16").forward(**inp)
+
+    def dist(l1, a1, l2, a2):
+        return max(float(np.abs(l1[mm] - l2[mm]).max()), float(np.abs(a1 - a2).max()))
+
+    to_oracle, to_bf16, oracle_to_bf16 = dist(logits, act, ol, oa), dist(logits, act, bl, ba), dist(ol, oa, bl, ba)
+    decided = O.top2_margin(ol, mm) > tol
+    agree = O.decision_agreement(ol[decided], logits[decided], mm[decided]) if decided.any() else 1.0
+    print(f"nvfp4 C3: max-abs to the nvfp4 oracle {to_oracle:.3e}, to the bf16 oracle {to_bf16:.3e} "
+          f"(nvfp4 oracle to bf16 oracle {oracle_to_bf16:.3e}), decisions where margin>{tol} {agree:.3f}, "
+          f"agreement with bf16 {O.decision_agreement(bl, logits, mm):.3f}")
+    assert agree == 1.0
+    assert to_bf16 <= tol, to_bf16
+    assert to_bf16 <= oracle_to_bf16 + 0.05, (to_bf16, oracle_to_bf16)
+    assert to_oracle <= 2 * tol, to_oracle
+    assert np.array_equal(logits[~mm], np.full((~mm).sum(), -1e4, np.float32))
 
 
 def test_serving_lanes_run_concurrently_with_identical_results():
