@@ -19,6 +19,14 @@
 //    columns [0, 64), which chunk 0's scores free before its P is released.
 //  * warp 1: key-validity bits (one word per 32 keys) and, for the head's
 //    selected query rows, the gather of Q into the swizzled layout.
+//  * split CTAs: when the (query tile, head, sequence) grid is smaller than
+//    the GPU (one long sequence), a cluster of 2 or 4 CTAs shares each query
+//    tile, each CTA taking a contiguous share of its key chunks.  The CTAs
+//    push each row's max to one another (st.async into the peers' shared
+//    memory, counted on their mbarriers), so all use the row's true max; each
+//    then sums p and accumulates O over its own keys, and CTA r of n gathers
+//    columns [64r/n, 64(r+1)/n) of O and the row sums from the others, adding
+//    the n partials in rank order.
 //  * warps 2-9: two threads per query row (warps 2-5 and 6-9 cover the four
 //    TMEM lane quarters twice), each owning 32 of every 64 key columns.
 //    Pass 1 reads the row's scores from TMEM and takes the max over visible
@@ -66,24 +74,34 @@ constexpr float kScaleLog2 = 0.125f * 1.4426950408889634f;  // 1/sqrt(64) * log2
 constexpr uint32_t kIdescPV = idesc_bf16(128, 64) | (1u << 16);
 
 // Shared memory (from a 1024-aligned base): Q, the K region, the V chunks,
-// then barriers, key bits, the TMEM slot and the half-row reductions.  Once
-// every score MMA has completed, Q and the K region hold the four P tiles
-// (hi and lo, two buffers), hence a K region of at least 6 chunks.
+// the partial O columns received from the other CTAs of a split tile, then
+// barriers, key bits, the TMEM slot and the row reductions.  Once every score
+// MMA has completed, Q and the K region hold the four P tiles (hi and lo, two
+// buffers), hence a K region of at least 6 chunks.
+constexpr int kMaxSplit = 4;
+constexpr uint32_t kBarBytes = 6144;
 struct Layout {
-  uint32_t k, v, bars, total;
+  uint32_t k, v, recv, bars, total;
 };
 __host__ __device__ constexpr uint32_t kregion(int chunks) { return (chunks > 6 ? chunks : 6) * kChunkBytes; }
-__host__ __device__ constexpr Layout layout(int chunks) {
+__host__ __device__ constexpr uint32_t recv_bytes(int split) { return (split - 1) * kTq * (64 / split) * 4; }
+__host__ __device__ constexpr Layout layout(int chunks, int split) {
   return Layout{kQBytes, kQBytes + kregion(chunks), kQBytes + kregion(chunks) + chunks * kChunkBytes,
-                kQBytes + kregion(chunks) + chunks * kChunkBytes + 4096};
+                kQBytes + kregion(chunks) + chunks * kChunkBytes + recv_bytes(split),
+                kQBytes + kregion(chunks) + chunks * kChunkBytes + recv_bytes(split) + kBarBytes};
 }
 struct Bars {
   uint64_t q, k[kMaxChunks], v[kMaxChunks], s[kMaxChunks / 2], p[2], pv[2], o;
+  uint64_t xm, xo;  // split tiles: the other CTAs' row maxima / O columns and sums arrived
   uint32_t key_bits[2 * kMaxChunks];
   uint32_t tmem_slot, failed;
   float red_max[2][kTq], red_sum[2][kTq];  // the two half-rows' max and sum
+  float peer_max[kMaxSplit - 1][kTq], peer_sum[kMaxSplit - 1][kTq];
 };
-static_assert(sizeof(Bars) <= 4096, "barrier block");
+static_assert(sizeof(Bars) <= kBarBytes, "barrier block");
+
+// Slot of sender s in receiver r's arrays (the receiver itself has none).
+__host__ __device__ constexpr int peer_slot(int s, int r) { return s < r ? s : s - 1; }
 
 // Keys [kbeg, kend) that the CTA's queries q0 .. q0+127 can see.
 __host__ __device__ inline void key_span(const AttnParams& p, int q0, int& kbeg, int& kend) {
@@ -163,20 +181,31 @@ DEVI uint32_t sw128_offset(int r, int j) { return (r >> 3) * 1024 + (r & 7) * 12
 
 }  // namespace
 
+template <int SPLIT>
 __global__ void __launch_bounds__(kThreads, 2)
     attention_tc_kernel(const __grid_constant__ CUtensorMap qkv_map, const AttnParams p, int max_chunks) {
+  constexpr int W = 64 / SPLIT;  // output columns gathered by each CTA of a split tile
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  const Layout L = layout(max_chunks);
+  const Layout L = layout(max_chunks, SPLIT);
   uint8_t* sQ = smem;
   uint8_t* sK = smem + L.k;
   uint8_t* sV = smem + L.v;
+  float* recv = reinterpret_cast<float*>(smem + L.recv);  // [SPLIT-1][kTq][W]
   Bars& B = *reinterpret_cast<Bars*>(smem + L.bars);
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int q0 = blockIdx.x * kTq, h = blockIdx.y, b = blockIdx.z;
+  const int rank = SPLIT > 1 ? (int)(blockIdx.x % SPLIT) : 0;
+  const int q0 = (blockIdx.x / SPLIT) * kTq, h = blockIdx.y, b = blockIdx.z;
   int kbeg, kend;
   key_span(p, q0, kbeg, kend);
+  {  // this CTA's share of the tile's key chunks
+    const int all = (kend - kbeg + kKc - 1) / kKc;
+    const int c0 = rank * all / SPLIT, c1 = (rank + 1) * all / SPLIT;
+    const int end = kbeg + c1 * kKc < kend ? kbeg + c1 * kKc : kend;
+    kbeg += c0 * kKc;
+    kend = end > kbeg ? end : kbeg;
+  }
   const int nk = kend - kbeg;
   const int chunks = (nk + kKc - 1) / kKc;
   const int blocks = (chunks + 1) / 2;
@@ -196,16 +225,25 @@ __global__ void __launch_bounds__(kThreads, 2)
     }
     mbar_init(&B.o, 1);
     B.failed = 0;
+    if (SPLIT > 1) {  // the bytes the other CTAs will push
+      mbar_init(&B.xm, 1);
+      mbar_init(&B.xo, 1);
+      mbar_expect_tx(&B.xm, (SPLIT - 1) * kTq * 4);
+      mbar_expect_tx(&B.xo, (SPLIT - 1) * kTq * (W + 1) * 4);
+    }
     fence_mbar_init();
     prefetch_tensormap(&qkv_map);
   }
-  __syncthreads();
+  if (SPLIT > 1)
+    cluster_sync_all();  // every CTA's barriers exist before any st.async
+  else
+    __syncthreads();
   griddep_wait();
 
   if (warp == 0) {
     if (lane == 0) {
       const uint64_t pol = policy_evict_first();
-      if (!p.q_pos) {
+      if (!p.q_pos && chunks > 0) {
         mbar_expect_tx(&B.q, kQBytes);
         tma_load_3d(sQ, &qkv_map, &B.q, h * 64, q0, b, pol);
         tma_load_3d(sQ + kQBytes / 2, &qkv_map, &B.q, h * 64, q0 + 64, b, pol);
@@ -233,7 +271,7 @@ __global__ void __launch_bounds__(kThreads, 2)
       const uint32_t bits = __ballot_sync(0xffffffffu, valid[w] != 0);
       if (lane == 0 && w < 2 * chunks) B.key_bits[w] = bits;
     }
-    if (p.q_pos) {  // selected query rows (head layer): gather Q, zeros past nq
+    if (p.q_pos && chunks > 0) {  // selected query rows (head layer): gather Q, zeros past nq
       for (int it = lane; it < kTq * 8; it += 32) {
         const int r = it >> 3, j = it & 7, qi = q0 + r;
         uint4 v = make_uint4(0, 0, 0, 0);
@@ -256,7 +294,7 @@ __global__ void __launch_bounds__(kThreads, 2)
 
   if (tid == 0) {
     // ---- MMA issue: scores for every 128 keys, then O += P V per chunk
-    bool ok = mbar_wait(&B.q, 0, limit);
+    bool ok = chunks == 0 || mbar_wait(&B.q, 0, limit);
     const uint64_t qd = sw128_desc(smem_u32(sQ));
     for (int j = 0; ok && j < blocks; ++j) {
       ok = mbar_wait(&B.k[2 * j], 0, limit) && (2 * j + 1 >= chunks || mbar_wait(&B.k[2 * j + 1], 0, limit));
@@ -324,6 +362,16 @@ __global__ void __launch_bounds__(kThreads, 2)
     B.red_max[half][row] = m;
     softmax_sync();
     m = fmaxf(B.red_max[0][row], B.red_max[1][row]);
+    if (SPLIT > 1) {  // the row's max over every CTA of the tile
+      if (half == 0)
+        for (int r = 0; r < SPLIT; ++r)
+          if (r != rank)
+            st_async_f32(mapa_shared(smem_u32(&B.peer_max[peer_slot(rank, r)][row]), r), m,
+                         mapa_shared(smem_u32(&B.xm), r));
+      if (!__all_sync(0xffffffffu, mbar_wait_cluster(&B.xm, 0, limit))) ok = false;
+#pragma unroll
+      for (int s = 0; s < SPLIT - 1; ++s) m = fmaxf(m, B.peer_max[s][row]);
+    }
     const float ms = m == -INFINITY ? 0.f : m * kScaleLog2;
     float l = 0.f;
     for (int c = 0; ok && c < chunks; ++c) {
@@ -356,34 +404,84 @@ __global__ void __launch_bounds__(kThreads, 2)
     softmax_sync();
     l = B.red_sum[0][row] + B.red_sum[1][row];
     if (ok) ok = __all_sync(0xffffffffu, mbar_wait(&B.o, 0, limit));
-    if (ok && live) {
+    // this CTA's O for the thread's 32 columns (zeros without keys)
+    uint32_t r[32];
+    if (ok && live && chunks > 0) {
       tc_fence_after();
-      uint32_t r[32];
       tmem_ld32(taddr, r);
       tmem_wait_ld();
-      if (qi < p.nq) {
-        const float inv = l > 0.f ? 1.f / l : 0.f;
-        uint4* dst = reinterpret_cast<uint4*>(p.out + ((size_t)b * p.nq + qi) * p.ld_out + h * 64 + 32 * half);
+    } else {
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          const uint32_t* x = r + 8 * j;
-          dst[j] = make_uint4(pack2(__uint_as_float(x[0]) * inv, __uint_as_float(x[1]) * inv),
-                              pack2(__uint_as_float(x[2]) * inv, __uint_as_float(x[3]) * inv),
-                              pack2(__uint_as_float(x[4]) * inv, __uint_as_float(x[5]) * inv),
-                              pack2(__uint_as_float(x[6]) * inv, __uint_as_float(x[7]) * inv));
+      for (int j = 0; j < 32; ++j) r[j] = 0u;
+    }
+    if (SPLIT > 1) {
+      // push the columns other CTAs gather, and the row sum; then gather ours
+#pragma unroll
+      for (int t = 0; t < 32 / W; ++t) {
+        const int owner = (32 * half) / W + t;
+        if (owner == rank) continue;
+        const uint32_t dst = mapa_shared(smem_u32(recv + ((size_t)peer_slot(rank, owner) * kTq + row) * W), owner);
+        const uint32_t bar = mapa_shared(smem_u32(&B.xo), owner);
+#pragma unroll
+        for (int j = 0; j < W; j += 4)
+          st_async_f32x4(dst + 4 * j, __uint_as_float(r[t * W + j]), __uint_as_float(r[t * W + j + 1]),
+                         __uint_as_float(r[t * W + j + 2]), __uint_as_float(r[t * W + j + 3]), bar);
+      }
+      if (half == 0)
+        for (int q = 0; q < SPLIT; ++q)
+          if (q != rank)
+            st_async_f32(mapa_shared(smem_u32(&B.peer_sum[peer_slot(rank, q)][row]), q), l,
+                         mapa_shared(smem_u32(&B.xo), q));
+      if (!__all_sync(0xffffffffu, mbar_wait_cluster(&B.xo, 0, limit))) ok = false;
+      const int mine = (rank * W) / 32, cofs = (rank * W) % 32;
+      if (ok && half == mine && qi < p.nq) {
+        // this CTA's partial, then the others' in rank order
+        float lt = l;
+        for (int q = 0; q < SPLIT; ++q)
+          if (q != rank) lt += B.peer_sum[peer_slot(q, rank)][row];
+        const float inv = lt > 0.f ? 1.f / lt : 0.f;
+        uint4* dst = reinterpret_cast<uint4*>(p.out + ((size_t)b * p.nq + qi) * p.ld_out + h * 64 + rank * W);
+#pragma unroll
+        for (int j8 = 0; j8 < W / 8; ++j8) {
+          float o[8];
+#pragma unroll
+          for (int j = 0; j < 8; ++j) o[j] = __uint_as_float(cofs ? r[(32 - W) + 8 * j8 + j] : r[8 * j8 + j]);
+          for (int q = 0; q < SPLIT; ++q) {
+            if (q == rank) continue;
+            const float4* src = reinterpret_cast<const float4*>(recv + ((size_t)peer_slot(q, rank) * kTq + row) * W + 8 * j8);
+            const float4 a = src[0], c = src[1];
+            o[0] += a.x; o[1] += a.y; o[2] += a.z; o[3] += a.w;
+            o[4] += c.x; o[5] += c.y; o[6] += c.z; o[7] += c.w;
+          }
+          dst[j8] = make_uint4(pack2(o[0] * inv, o[1] * inv), pack2(o[2] * inv, o[3] * inv),
+                               pack2(o[4] * inv, o[5] * inv), pack2(o[6] * inv, o[7] * inv));
         }
       }
-    } else if (!ok) {
+    } else if (ok && live && qi < p.nq) {
+      const float inv = l > 0.f ? 1.f / l : 0.f;
+      uint4* dst = reinterpret_cast<uint4*>(p.out + ((size_t)b * p.nq + qi) * p.ld_out + h * 64 + 32 * half);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const uint32_t* x = r + 8 * j;
+        dst[j] = make_uint4(pack2(__uint_as_float(x[0]) * inv, __uint_as_float(x[1]) * inv),
+                            pack2(__uint_as_float(x[2]) * inv, __uint_as_float(x[3]) * inv),
+                            pack2(__uint_as_float(x[4]) * inv, __uint_as_float(x[5]) * inv),
+                            pack2(__uint_as_float(x[6]) * inv, __uint_as_float(x[7]) * inv));
+      }
+    }
+    if (!ok) {
       record_status(p.status, kStatusAttnTimeout);
       atomicExch(&B.failed, 1u);
     }
   }
 
   // ---- teardown: after a failure, wait (bounded) for this CTA's copies and
-  // MMAs before its shared memory and TMEM are released
+  // MMAs before its shared memory and TMEM are released; a split tile's CTAs
+  // leave together, after every push into their shared memory
   __syncthreads();
+  if (SPLIT > 1) cluster_sync_all();
   if (tid == 0 && B.failed) {
-    if (!p.q_pos) mbar_wait(&B.q, 0, limit);
+    if (!p.q_pos && chunks > 0) mbar_wait(&B.q, 0, limit);
     for (int c = 0; c < chunks; ++c) {
       mbar_wait(&B.k[c], 0, limit);
       mbar_wait(&B.v[c], 0, limit);
@@ -411,6 +509,58 @@ int attention_chunks(const AttnParams& p) {
   return most;
 }
 
+namespace {
+
+template <int SPLIT>
+cudaError_t launch_split(const AttnParams& p, const CUtensorMap& qkv_map, int batch, int heads, int chunks,
+                         cudaStream_t stream, bool pdl) {
+  const int share = (chunks + SPLIT - 1) / SPLIT;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(((p.nq + kTq - 1) / kTq) * SPLIT, heads, batch);
+  cfg.blockDim = dim3(kThreads, 1, 1);
+  cfg.dynamicSmemBytes = layout(share, SPLIT).total + 1024;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[2];
+  int n = 0;
+  if (pdl) {
+    attr[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[n].val.programmaticStreamSerializationAllowed = 1;
+    ++n;
+  }
+  if (SPLIT > 1) {
+    attr[n].id = cudaLaunchAttributeClusterDimension;
+    attr[n].val.clusterDim.x = SPLIT;
+    attr[n].val.clusterDim.y = 1;
+    attr[n].val.clusterDim.z = 1;
+    ++n;
+  }
+  cfg.attrs = attr;
+  cfg.numAttrs = n;
+  return cudaLaunchKernelEx(&cfg, attention_tc_kernel<SPLIT>, qkv_map, p, share);
+}
+
+template <int SPLIT>
+cudaError_t prepare_split() {
+  cudaError_t err = cudaFuncSetAttribute(attention_tc_kernel<SPLIT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)layout(kMaxChunks, SPLIT).total + 1024);
+  // all of the unified L1 / shared storage as shared memory, so that two
+  // CTAs of up to four chunks each fit on one SM
+  if (err == cudaSuccess)
+    err = cudaFuncSetAttribute(attention_tc_kernel<SPLIT>, cudaFuncAttributePreferredSharedMemoryCarveout,
+                               (int)cudaSharedmemCarveoutMaxShared);
+  return err;
+}
+
+}  // namespace
+
+int attention_split(int base_ctas, int chunks, int sm_count) {
+  // Fewer (tile, head, sequence) CTAs than SMs: share each tile's chunks over
+  // a cluster, keeping at least two chunks per CTA on the widest tile.
+  if (base_ctas >= sm_count) return 1;
+  if (chunks >= 8 && 2 * base_ctas < sm_count) return 4;
+  return chunks >= 4 ? 2 : 1;
+}
+
 cudaError_t launch_attention(const AttnParams& p, const CUtensorMap& qkv_map, int batch, int heads,
                              cudaStream_t stream, bool pdl) {
   if ((p.window >= 0 && p.q_pos) || p.nq < 1 || p.s < 1 || batch < 1 || heads < 1) return cudaErrorInvalidValue;
@@ -418,6 +568,7 @@ cudaError_t launch_attention(const AttnParams& p, const CUtensorMap& qkv_map, in
   if (chunks < 1 || chunks > kMaxChunks) return cudaErrorInvalidValue;
   static std::mutex mu;
   static uint64_t ready = 0;
+  static int sms[64] = {0};
   int dev = 0;
   cudaError_t err = cudaGetDevice(&dev);
   if (err != cudaSuccess) return err;
@@ -425,28 +576,23 @@ cudaError_t launch_attention(const AttnParams& p, const CUtensorMap& qkv_map, in
   {
     std::lock_guard<std::mutex> lock(mu);
     if (!(ready >> dev & 1)) {
-      err = cudaFuncSetAttribute(attention_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 (int)layout(kMaxChunks).total + 1024);
-      // all of the unified L1 / shared storage as shared memory, so that two
-      // CTAs of up to four chunks each fit on one SM
-      if (err == cudaSuccess)
-        err = cudaFuncSetAttribute(attention_tc_kernel, cudaFuncAttributePreferredSharedMemoryCarveout,
-                                   (int)cudaSharedmemCarveoutMaxShared);
+      err = prepare_split<1>();
+      if (err == cudaSuccess) err = prepare_split<2>();
+      if (err == cudaSuccess) err = prepare_split<4>();
+      if (err == cudaSuccess) err = cudaDeviceGetAttribute(&sms[dev], cudaDevAttrMultiProcessorCount, dev);
       if (err != cudaSuccess) return err;
       ready |= uint64_t(1) << dev;
     }
   }
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3((p.nq + kTq - 1) / kTq, heads, batch);
-  cfg.blockDim = dim3(kThreads, 1, 1);
-  cfg.dynamicSmemBytes = layout(chunks).total + 1024;
-  cfg.stream = stream;
-  cudaLaunchAttribute attr;
-  attr.id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr.val.programmaticStreamSerializationAllowed = 1;
-  cfg.attrs = &attr;
-  cfg.numAttrs = pdl ? 1 : 0;
-  return cudaLaunchKernelEx(&cfg, attention_tc_kernel, qkv_map, p, chunks);
+  const long long base = (long long)((p.nq + kTq - 1) / kTq) * heads * batch;
+  switch (attention_split(base > (1 << 30) ? (1 << 30) : (int)base, chunks, sms[dev])) {
+    case 4:
+      return launch_split<4>(p, qkv_map, batch, heads, chunks, stream, pdl);
+    case 2:
+      return launch_split<2>(p, qkv_map, batch, heads, chunks, stream, pdl);
+    default:
+      return launch_split<1>(p, qkv_map, batch, heads, chunks, stream, pdl);
+  }
 }
 
 }  // namespace laya

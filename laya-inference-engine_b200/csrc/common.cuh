@@ -258,6 +258,36 @@ DEVI float4 ld_dsmem_f32x4(uint32_t addr) {
                : "r"(addr));
   return v;
 }
+// Asynchronous store into another CTA's shared memory (cluster address) that
+// counts its bytes on that CTA's mbarrier (cluster address).
+DEVI void st_async_f32(uint32_t addr, float v, uint32_t bar) {
+  asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.f32 [%0], %1, [%2];" ::"r"(addr), "f"(v),
+               "r"(bar)
+               : "memory");
+}
+DEVI void st_async_f32x4(uint32_t addr, float a, float b, float c, float d, uint32_t bar) {
+  asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.v4.f32 [%0], {%1, %2, %3, %4}, [%5];" ::"r"(
+                   addr),
+               "f"(a), "f"(b), "f"(c), "f"(d), "r"(bar)
+               : "memory");
+}
+// mbarrier wait that also acquires what other CTAs of the cluster stored
+// with st.async before completing its transaction bytes; false after limit_ns.
+DEVI bool mbar_wait_cluster(uint64_t* bar, uint32_t parity, uint64_t limit_ns) {
+  const uint32_t addr = smem_u32(bar);
+  const uint64_t t0 = globaltimer();
+  while (true) {
+    uint32_t ok;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n"
+        " selp.u32 %0, 1, 0, p;\n}\n"
+        : "=r"(ok)
+        : "r"(addr), "r"(parity)
+        : "memory");
+    if (ok) return true;
+    if (globaltimer() - t0 > limit_ns) return false;
+  }
+}
 DEVI uint32_t cluster_ctarank() {
   uint32_t r;
   asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
