@@ -235,7 +235,10 @@ def test_nvfp4_activation_quantiser_is_bit_exact(intermediate):
         nf.run(nf.capture(b, s, k, False), pack(items, b, s, k, cfg.pad_token_id))
         T, K = b * s, intermediate
         col_blocks = 4 * ((K + 255) // 256)
-        rows_per_block = 128  # token tile of the Wo2 projection at 384 tokens
+        # token tile of the Wo2 projection at 384 tokens: 128, or 64 when the
+        # 128-token grid would leave SMs idle (gemm_plan)
+        sms = torch.cuda.get_device_properties(0).multi_processor_count
+        rows_per_block = 64 if (cfg.hidden // 128) * ((b * s + 127) // 128) < sms else 128
         x = bf16_of(nf.read_buffer("g", (T, K), np.uint16))
         nib = nf.read_buffer("x4", (T, K // 2), np.uint8)
         sf_bytes = ((T + rows_per_block - 1) // rows_per_block) * col_blocks * 512
