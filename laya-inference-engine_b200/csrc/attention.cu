@@ -20,8 +20,9 @@
 //  * warp 1: key-validity bits (one word per 32 keys) and, for the head's
 //    selected query rows, the gather of Q into the swizzled layout.
 //  * split CTAs: when the (query tile, head, sequence) grid is smaller than
-//    the GPU (one long sequence), a cluster of 2 or 4 CTAs shares each query
-//    tile, each CTA taking a contiguous share of its key chunks.  The CTAs
+//    the GPU (one long sequence), a cluster of 2 CTAs (the code takes up to
+//    4) shares each query tile, each CTA taking a contiguous share of its key
+//    chunks.  The CTAs
 //    push each row's max to one another (st.async into the peers' shared
 //    memory, counted on their mbarriers), so all use the row's true max; each
 //    then sums p and accumulates O over its own keys, and CTA r of n gathers
@@ -555,10 +556,11 @@ cudaError_t prepare_split() {
 
 int attention_split(int base_ctas, int chunks, int sm_count) {
   // Fewer (tile, head, sequence) CTAs than SMs: share each tile's chunks over
-  // a cluster, keeping at least two chunks per CTA on the widest tile.
-  if (base_ctas >= sm_count) return 1;
-  if (chunks >= 8 && 2 * base_ctas < sm_count) return 4;
-  return chunks >= 4 ? 2 : 1;
+  // a pair of CTAs, at least two chunks each on the widest tile.  Measured on
+  // C3 (64 tiles x heads, 4 or 8 chunks): pairs 1.757 ms per forward, no
+  // split 1.769, clusters of 4 for the 8-chunk global layers 1.801 (their two
+  // exchanges cost more than the shorter second pass saves).
+  return base_ctas < sm_count && chunks >= 4 ? 2 : 1;
 }
 
 cudaError_t launch_attention(const AttnParams& p, const CUtensorMap& qkv_map, int batch, int heads,
@@ -578,7 +580,6 @@ cudaError_t launch_attention(const AttnParams& p, const CUtensorMap& qkv_map, in
     if (!(ready >> dev & 1)) {
       err = prepare_split<1>();
       if (err == cudaSuccess) err = prepare_split<2>();
-      if (err == cudaSuccess) err = prepare_split<4>();
       if (err == cudaSuccess) err = cudaDeviceGetAttribute(&sms[dev], cudaDevAttrMultiProcessorCount, dev);
       if (err != cudaSuccess) return err;
       ready |= uint64_t(1) << dev;
@@ -586,8 +587,6 @@ cudaError_t launch_attention(const AttnParams& p, const CUtensorMap& qkv_map, in
   }
   const long long base = (long long)((p.nq + kTq - 1) / kTq) * heads * batch;
   switch (attention_split(base > (1 << 30) ? (1 << 30) : (int)base, chunks, sms[dev])) {
-    case 4:
-      return launch_split<4>(p, qkv_map, batch, heads, chunks, stream, pdl);
     case 2:
       return launch_split<2>(p, qkv_map, batch, heads, chunks, stream, pdl);
     default:

@@ -40,7 +40,7 @@ cudaError_t launch_attention(const AttnParams& p, const CUtensorMap& qkv_map, in
                              cudaStream_t stream, bool pdl);
 // Chunks of 64 keys the widest query tile of p sees (the kernel takes <= 8).
 int attention_chunks(const AttnParams& p);
-// CTAs that share one query tile's key chunks (1, 2 or 4) for a grid of
+// CTAs that share one query tile's key chunks (1 or 2) for a grid of
 // base_ctas (tile, head, sequence) CTAs on sm_count SMs.
 int attention_split(int base_ctas, int chunks, int sm_count);
 cudaError_t launch_norm(const NormParams& p, cudaStream_t stream, bool pdl);
