@@ -347,6 +347,8 @@ void validate_cfg(const laya_b200_config& c) {
 
 // Rotary tables like transformers' default rope: inv_freq in fp32, the angle
 // pos*inv_freq in fp32, cos/sin of that fp32 angle.
+// Columns i and i + 32 hold the same angle (cat(freqs, freqs)); the QKV
+// epilogue's rotary tiles rely on it and read only the first 32.
 void rope_tables(float theta, int max_len, std::vector<float>& cs, std::vector<float>& sn) {
   cs.assign((size_t)max_len * 64, 0.f);
   sn.assign((size_t)max_len * 64, 0.f);

@@ -396,8 +396,10 @@ DEVI void tile_epilogue_wide(const GemmParams& p, const CUtensorMap* omap, uint3
   if (tile_n * 128 + 128 <= p.rope_cols) {
     // rotary tile (two q or k heads): a thread takes rows r0..r0+3 (d0 < 32),
     // their partners r0+32.., and the same two row groups of the second head
-    // (+64), for tokens tid/8, +32, ...: one cos / sin pair (d0 and d0+32)
-    // serves all four, and a thread's four tokens are loaded in one batch.
+    // (+64), for tokens tid/8, +32, ...: one cos / sin quad serves all four,
+    // since the tables repeat their first 32 columns (the rotary embedding's
+    // cat(freqs, freqs), built so by rope_tables), and a thread's four tokens
+    // are loaded in one batch.
     const int r0 = 4 * (tid & 7);
     float ws[4][4];
 #pragma unroll
@@ -409,20 +411,20 @@ DEVI void tile_epilogue_wide(const GemmParams& p, const CUtensorMap* omap, uint3
       }
     }
     constexpr int RT = BN / (THREADS / 8);  // tokens per thread
-    float4 c0[RT], c1[RT], s0[RT], s1[RT];
+    float4 c0[RT], s0[RT];
 #pragma unroll
     for (int u = 0; u < RT; ++u) {
       const int pos = (m_base + (tid >> 3) + u * (THREADS / 8)) % p.rope_seq;
       c0[u] = *reinterpret_cast<const float4*>(p.rope_cos + (size_t)pos * 64 + r0);
-      c1[u] = *reinterpret_cast<const float4*>(p.rope_cos + (size_t)pos * 64 + r0 + 32);
       s0[u] = *reinterpret_cast<const float4*>(p.rope_sin + (size_t)pos * 64 + r0);
-      s1[u] = *reinterpret_cast<const float4*>(p.rope_sin + (size_t)pos * 64 + r0 + 32);
     }
 #pragma unroll
     for (int u = 0; u < RT; ++u) {
       const int tok = (tid >> 3) + u * (THREADS / 8);
-      const float cl[4] = {c0[u].x, c0[u].y, c0[u].z, c0[u].w}, ch[4] = {c1[u].x, c1[u].y, c1[u].z, c1[u].w};
-      const float sl[4] = {s0[u].x, s0[u].y, s0[u].z, s0[u].w}, sh[4] = {s1[u].x, s1[u].y, s1[u].z, s1[u].w};
+      const float cl[4] = {c0[u].x, c0[u].y, c0[u].z, c0[u].w};
+      const float sl[4] = {s0[u].x, s0[u].y, s0[u].z, s0[u].w};
+      const float* ch = cl;
+      const float* sh = sl;
       const float sc = KIND == kKindNvfp4 ? S[tok] * tsc : KIND == kKindFp8 ? S[tok] : 1.f;
 #pragma unroll
       for (int hd = 0; hd < 2; ++hd) {
