@@ -311,3 +311,16 @@ def test_prepare_without_tokenizer_names_what_is_missing():
     engine.tokenizer = None
     with pytest.raises(RuntimeError, match="tokenizer"):
         engine.predict({}, [{"id": "q"}])
+
+
+@pytest.mark.parametrize("changes, message", [
+    ({"max_len": 768}, "max_len"),      # attention keeps a query's 512 scores in tensor memory
+    ({"max_len": 0}, "max_len"),
+    ({"head_dim": 32}, "head dimension"),
+])
+def test_config_validation_names_the_limit(changes, message):
+    from dataclasses import replace
+    from laya_b200.config import LAYA
+    with pytest.raises(ValueError, match=message):
+        replace(LAYA, **changes).validate()
+    LAYA.validate()
