@@ -70,7 +70,7 @@ def parse():
     ap.add_argument("--no-configs", action="store_true", help="c1: skip the C2 / C3 / C4 legs")
     ap.add_argument("--no-reference-gpu", action="store_true", help="c1: skip the reference-on-this-GPU leg")
     ap.add_argument("--config-steps", type=int, default=20,
-                    help="c1: timed steps of each of the C2 / C3 / C4 legs (C4: a quarter of it, at least 4)")
+                    help="c1: timed steps of the C2 / C3 legs (C4: at least 50)")
     ap.add_argument("--workload", default="c1", choices=["c1", "c2", "c3", "c4"],
                     help="c1 (default, the contract line): b=1 s=64 noul; c2: FP8 16x96; c3: NVFP4 1x512; "
                          "c4: FP8 64 questions s~U[32,512] bucketed by 32, sharded over ranks")
@@ -257,6 +257,31 @@ def cpu_baseline(cfg, seconds, precision="bf16", max_steps=None, warmup=1, weigh
             "sample": f"{len(times)} forwards of b=1 s=64 noul (one decision each), {total:.1f} s, {what}, "
                       f"on {os.cpu_count()} host cores",
             "ms_per_forward": 1000 * total / len(times), "steps": len(times), "warmup": warm}
+
+
+def cpu_fp32_restatement(cfg, seconds, weights):
+    """BASELINE config 0's "CPU fp32", labelled as a restatement: the oracle
+    port (oracle/laya_oracle.py) with every Linear in fp32 (bf16-valued
+    weights, fp32 accumulation) on all host cores, a bounded sample of the
+    same C0 request."""
+    import torch
+    from oracle.laya_oracle import Oracle
+    torch.set_num_threads(os.cpu_count() or 1)
+    _, inp = workload(cfg)
+    orc = Oracle(weights, cfg, "bf16")
+    orc.forward(**inp)
+    times = []
+    t_end = time.perf_counter() + seconds
+    while time.perf_counter() < t_end:
+        t0 = time.perf_counter()
+        orc.forward(**inp)
+        times.append(time.perf_counter() - t0)
+    total = sum(times)
+    return {"value": len(times) / total, "unit": UNIT, "cores": torch.get_num_threads(), "kind": "port",
+            "ms_per_forward": 1000 * total / len(times),
+            "sample": f"{len(times)} forwards of b=1 s=64 noul, {total:.1f} s, oracle/laya_oracle.py restatement "
+                      "with fp32 Linears (fp32 accumulation of the bf16-valued weights), labelled as a "
+                      f"restatement, on {os.cpu_count()} host cores"}
 
 
 def dist_setup(n):
@@ -643,7 +668,7 @@ def main():
     configs = {}
     if not args.no_configs:
         for w in ("c2", "c3", "c4"):
-            n = args.config_steps if w != "c4" else max(4, args.config_steps // 4)
+            n = args.config_steps if w != "c4" else max(50, args.config_steps)  # C4: >= 50 steps
             configs[w] = measure_batched(w, cfg, weights, local, rank, world, dist, n, 3, lanes=1)
 
     ref_gpu = None
@@ -656,6 +681,7 @@ def main():
 
     if rank == 0:
         base = cpu_baseline(cfg, args.cpu_seconds, args.precision, weights=weights)
+        fp32 = cpu_fp32_restatement(cfg, min(5.0, args.cpu_seconds / 3), weights)
         cs = clocks.summary()
         line = {
             "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
@@ -679,7 +705,8 @@ def main():
                          "avg_launch_us": 1000 * gemm_ms / glaunch},
             "forward_roofline": {"bytes_alg": fwd_bytes, "achieved_gbs": fwd_achieved,
                                  "frac": fwd_achieved / peak},
-            "cpu_baseline": {k: base[k] for k in ("value", "unit", "cores", "kind", "sample")},
+            "cpu_baseline": {**{k: base[k] for k in ("value", "unit", "cores", "kind", "sample")},
+                             "fp32_restatement": fp32},
             **({"serving_lanes": lanes_line} if lanes_line else {}),
             "gpu_launches": kernels * args.steps,
             "kernels_per_forward": kernels,

@@ -32,3 +32,19 @@ def test_reference_arm_prints_the_contract_line():
     want = "reference" if laya_net.reference_src() is not None else "port"
     assert base["kind"] == want and base["cores"] >= 1 and base["value"] == line["value"]
     assert line["config"]["workload"].startswith("C1")
+
+
+def test_fp32_restatement_is_labelled_and_bounded():
+    """BASELINE config 0's "CPU fp32" figure, reported inside cpu_baseline as a
+    labelled restatement (the oracle with fp32 Linears), within its time bound."""
+    import time
+    sys.path.insert(0, str(ROOT))
+    sys.path.insert(0, str(ROOT / "laya-inference-engine_b200"))
+    import bench
+    from laya_b200.config import TINY
+    from laya_b200.weights import seeded_weights
+    t0 = time.perf_counter()
+    out = bench.cpu_fp32_restatement(TINY, 0.5, seeded_weights(TINY, seed=0))
+    assert time.perf_counter() - t0 < 30
+    assert out["kind"] == "port" and out["value"] > 0 and out["cores"] >= 1
+    assert "restatement" in out["sample"] and "fp32" in out["sample"]
