@@ -331,6 +331,62 @@ __global__ void __launch_bounds__(128) quant_nvfp4_kernel(const QuantParams p, i
   }
 }
 
+// The same quantisation with one warp per row, for large row counts (from
+// 2,048 rows): chunk c = lane + 32 i of 8 elements, so a 16-element block is
+// the chunk pair of lanes (2m, 2m+1) and its maximum takes one shuffle.
+// Arithmetic identical to quant_nvfp4_kernel.
+template <int CPL>
+__global__ void __launch_bounds__(256) quant_nvfp4_warp_kernel(const QuantParams p, int rows_per_block,
+                                                               int col_blocks) {
+  griddep_launch_dependents();
+  griddep_wait();
+  const int lane = threadIdx.x & 31, row = blockIdx.x * 8 + (threadIdx.x >> 5);
+  if (row >= p.rows) return;
+  const int chunks = p.k / 8;
+  const __nv_bfloat16* src = p.src + (size_t)row * p.k;
+  uint4 u[CPL];
+#pragma unroll
+  for (int i = 0; i < CPL; ++i) {
+    const int c = lane + 32 * i;
+    u[i] = c < chunks ? reinterpret_cast<const uint4*>(src)[c] : make_uint4(0, 0, 0, 0);
+  }
+  float amax = 0.f;
+#pragma unroll
+  for (int i = 0; i < CPL; ++i) {
+    const __nv_bfloat16* e = reinterpret_cast<const __nv_bfloat16*>(&u[i]);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) amax = fmaxf(amax, fabsf(__bfloat162float(e[j])));
+  }
+  amax = warp_max(amax);
+  const float outer = fmaxf(amax / (6.0f * 448.0f), 1e-20f);
+  if (lane == 0) p.scale[row] = outer;
+  const float o6 = 6.0f * outer, inv_o6 = 1.0f / o6;
+  uint8_t* q = p.q + (size_t)row * (p.k / 2);
+#pragma unroll
+  for (int i = 0; i < CPL; ++i) {
+    const int c = lane + 32 * i;
+    const __nv_bfloat16* e = reinterpret_cast<const __nv_bfloat16*>(&u[i]);
+    float x[8], bmax = 0.f;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      x[j] = __bfloat162float(e[j]);
+      bmax = fmaxf(bmax, fabsf(x[j]));
+    }
+    bmax = fmaxf(bmax, __shfl_xor_sync(0xffffffffu, bmax, 1));  // the lane pair of one 16-element block
+    if (c >= chunks) continue;
+    const float sc = fmaxf(div_rn_by(bmax, o6, inv_o6), 0.001953125f);  // 2^-9 floor
+    const uint8_t sc8 = (uint8_t)(f32x2_to_e4m3x2(sc, 0.f) & 0xFF);
+    const float scale = e4m3_value(sc8);
+    const float denom = scale * outer, inv_d = 1.0f / denom;
+    uint32_t w = 0;
+#pragma unroll
+    for (int j = 0; j < 8; j += 2)
+      w |= (uint32_t)f32x2_to_e2m1x2(div_rn_by(x[j], denom, inv_d), div_rn_by(x[j + 1], denom, inv_d)) << (4 * j);
+    reinterpret_cast<uint32_t*>(q)[c] = w;
+    if ((lane & 1) == 0) p.sf[sf_offset(row, c / 2, rows_per_block, col_blocks)] = sc8;
+  }
+}
+
 // ------------------------------------------------------------- host side
 
 namespace {
@@ -411,6 +467,23 @@ cudaError_t launch_quant_nvfp4(const QuantParams& p, int rows_per_block, int col
   if (p.k % 16 || p.k > 4096) return cudaErrorInvalidValue;
   QuantParams q = p;
   void* args[] = {&q, &rows_per_block, &col_blocks};
+  if (p.rows >= 2048) {  // a warp per row (same switch as the FP8 quantiser and the LayerNorm rows)
+    const int cpl = (p.k / 8 + 31) / 32;
+    const void* wk = cpl <= 4    ? (const void*)quant_nvfp4_warp_kernel<4>
+                     : cpl <= 8  ? (const void*)quant_nvfp4_warp_kernel<8>
+                     : cpl <= 12 ? (const void*)quant_nvfp4_warp_kernel<12>
+                                 : (const void*)quant_nvfp4_warp_kernel<16>;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((p.rows + 7) / 8, 1, 1);
+    cfg.blockDim = dim3(256, 1, 1);
+    cfg.stream = stream;
+    cudaLaunchAttribute attr;
+    attr.id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr.val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = &attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    return cudaLaunchKernelExC(&cfg, wk, args);
+  }
   const void* kern = p.k <= 1024   ? (const void*)quant_nvfp4_kernel<1>
                      : p.k <= 2048 ? (const void*)quant_nvfp4_kernel<2>
                      : p.k <= 3072 ? (const void*)quant_nvfp4_kernel<3>

@@ -86,6 +86,53 @@ __global__ void __launch_bounds__(128) quant_fp8_kernel(const QuantParams p) {
   if (tid == 0) p.scale[row] = scale;
 }
 
+// The same quantisation with one warp per row, for large row counts (from
+// 2,048 rows, where one CTA per row runs in several waves): chunk
+// c = lane + 32 i of 8 elements, every load in flight at once, the row
+// maximum a warp reduction.  Arithmetic identical to quant_fp8_kernel.
+template <int CPL>
+__global__ void __launch_bounds__(256) quant_fp8_warp_kernel(const QuantParams p) {
+  griddep_launch_dependents();
+  griddep_wait();
+  const int lane = threadIdx.x & 31, row = blockIdx.x * 8 + (threadIdx.x >> 5);
+  if (row >= p.rows) return;
+  const int chunks = p.k / 8;
+  const __nv_bfloat16* src = p.src + (size_t)row * p.k;
+  uint4 u[CPL];
+#pragma unroll
+  for (int i = 0; i < CPL; ++i) {
+    const int c = lane + 32 * i;
+    u[i] = c < chunks ? reinterpret_cast<const uint4*>(src)[c] : make_uint4(0, 0, 0, 0);
+  }
+  float amax = 0.f;
+#pragma unroll
+  for (int i = 0; i < CPL; ++i) {
+    const __nv_bfloat16* e = reinterpret_cast<const __nv_bfloat16*>(&u[i]);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) amax = fmaxf(amax, fabsf(__bfloat162float(e[j])));
+  }
+  amax = warp_max(amax);
+  const float scale = fmaxf(amax * kInvE4m3Max, 1e-12f), inv = 1.0f / scale;
+  uint8_t* dst = p.q + (size_t)row * p.k;
+#pragma unroll
+  for (int i = 0; i < CPL; ++i) {
+    const int c = lane + 32 * i;
+    if (c >= chunks) continue;
+    const __nv_bfloat16* e = reinterpret_cast<const __nv_bfloat16*>(&u[i]);
+    uint32_t w[2];
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+      float v[4];
+#pragma unroll
+      for (int t = 0; t < 4; ++t)
+        v[t] = fminf(fmaxf(div_rn_by(__bfloat162float(e[4 * j + t]), scale, inv), -448.f), 448.f);
+      w[j] = (uint32_t)f32x2_to_e4m3x2(v[0], v[1]) | ((uint32_t)f32x2_to_e4m3x2(v[2], v[3]) << 16);
+    }
+    reinterpret_cast<uint2*>(dst)[c] = make_uint2(w[0], w[1]);
+  }
+  if (lane == 0) p.scale[row] = scale;
+}
+
 // dst[r] = src[map[r]] for fp32 rows of width d (multiple of 4).
 __global__ void __launch_bounds__(256) gather_rows_kernel(float* dst, const float* src, const int* map, int rows,
                                                            int d) {
@@ -221,6 +268,10 @@ __global__ void __launch_bounds__(256) pack_fp8_rows_kernel(const __nv_bfloat16*
 // ------------------------------------------------------------------ launchers
 namespace {
 // One warp per row, `rows_per_block` rows (warps) per CTA.
+// Row count from which the row kernels with quantised outputs use a warp
+// per row instead of a CTA per row.
+constexpr int kWarpRowsFrom = 2048;
+
 cudaError_t launch_rows(const void* kern, void** args, int rows, size_t smem, cudaStream_t stream, bool pdl,
                         int rows_per_block = 8) {
   cudaLaunchConfig_t cfg = {};
@@ -252,8 +303,10 @@ cudaError_t launch_norm(const NormParams& p, cudaStream_t stream, bool pdl) {
     case 7: kern = (const void*)norm_kernel<7>; break;
     case 8: kern = (const void*)norm_kernel<8>; break;
   }
-  if ((p.out_fp8 || p.out_x4) && p.d % 256 == 0) {
-    // quantised outputs carry much more per-row work: one CTA per row
+  if ((p.out_fp8 || p.out_x4) && p.d % 256 == 0 && p.rows < kWarpRowsFrom) {
+    // quantised outputs carry much more per-row work: one CTA per row while
+    // that fits in about one wave; from 2,048 rows a warp per row
+    // (8,192-token FP8 forward: 9.03 -> 8.83 ms)
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(p.rows, 1, 1);
     cfg.blockDim = dim3(p.d / 8, 1, 1);
@@ -272,6 +325,14 @@ cudaError_t launch_quant_fp8(const QuantParams& p, cudaStream_t stream, bool pdl
   if (p.k % 8 || p.k > 4096) return cudaErrorInvalidValue;
   QuantParams q = p;
   void* args[] = {&q};
+  if (p.rows >= kWarpRowsFrom) {  // a warp per row (see launch_norm)
+    const int cpl = (p.k / 8 + 31) / 32;
+    const void* wk = cpl <= 4    ? (const void*)quant_fp8_warp_kernel<4>
+                     : cpl <= 8  ? (const void*)quant_fp8_warp_kernel<8>
+                     : cpl <= 12 ? (const void*)quant_fp8_warp_kernel<12>
+                                 : (const void*)quant_fp8_warp_kernel<16>;
+    return launch_rows(wk, args, p.rows, 0, stream, pdl, 8);
+  }
   const void* kern = p.k <= 1024   ? (const void*)quant_fp8_kernel<1>
                      : p.k <= 2048 ? (const void*)quant_fp8_kernel<2>
                      : p.k <= 3072 ? (const void*)quant_fp8_kernel<3>

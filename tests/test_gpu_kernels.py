@@ -160,8 +160,14 @@ def test_low_precision_qkv_stage_matches_oracle(precision):
     assert np.abs(logits[mm] - ol[mm]).max() <= tol and np.abs(act - oa).max() <= tol
 
 
-@pytest.mark.parametrize("intermediate", [384, 1920, 2624, 4096])
-def test_fp8_activation_quantiser_is_bit_exact(intermediate):
+# (batch, seq, lengths): 256 rows run one CTA per row, 2,048 rows a warp per row
+ROWS_SMALL = (2, 128, [128, 77])
+ROWS_LARGE = (4, 512, [512, 300, 512, 77])
+
+
+@pytest.mark.parametrize("intermediate, rows", [(384, ROWS_SMALL), (1920, ROWS_SMALL), (2624, ROWS_SMALL),
+                                                (4096, ROWS_SMALL), (2624, ROWS_LARGE), (4096, ROWS_LARGE)])
+def test_fp8_activation_quantiser_is_bit_exact(intermediate, rows):
     """The per-row e4m3 activation quantiser (quantization.py:20-29) on the
     attention output (k = hidden) and the GEGLU output (k = intermediate)
     against the oracle's torch restatement: scales and codes identical."""
@@ -171,8 +177,9 @@ def test_fp8_activation_quantiser_is_bit_exact(intermediate):
     w = seeded_weights(cfg, seed=5)
     nf = NativeForward(0, cfg, w, "fp8", max_batch=4, max_options=8)
     try:
-        b, s, k = 2, 128, 4
-        items = synthetic_items([128, 77], ["choice", "score"], seed=12, vocab=cfg.vocab)
+        b, s, lengths = rows
+        k = 4
+        items = synthetic_items(lengths, ["choice", "score", "noul", "choice"][:b], seed=12, vocab=cfg.vocab)
         nf.run(nf.capture(b, s, k, False), pack(items, b, s, k, cfg.pad_token_id))
         T = b * s
         for src, q, sc, width in (("attn", "a8", "a8s", cfg.hidden), ("g", "g8", "g8s", intermediate)):
@@ -219,8 +226,9 @@ def _sf_offset(row, g, rows_per_block, col_blocks):
     return (rb * col_blocks + (g >> 2)) * 512 + (r & 31) * 16 + (r >> 5) * 4 + (g & 3)
 
 
-@pytest.mark.parametrize("intermediate", [384, 1920, 2624, 4096])
-def test_nvfp4_activation_quantiser_is_bit_exact(intermediate):
+@pytest.mark.parametrize("intermediate, rows", [(384, ROWS_SMALL), (1920, ROWS_SMALL), (2624, ROWS_SMALL),
+                                                (4096, ROWS_SMALL), (2624, ROWS_LARGE)])
+def test_nvfp4_activation_quantiser_is_bit_exact(intermediate, rows):
     """The per-row NVFP4 activation quantiser (nvfp4.py:36-51 with a per-row
     outer scale) on the GEGLU output against the oracle's restatement: outer
     scales, e4m3 block scales and e2m1 codes identical."""
@@ -230,8 +238,9 @@ def test_nvfp4_activation_quantiser_is_bit_exact(intermediate):
     w = seeded_weights(cfg, seed=6)
     nf = NativeForward(0, cfg, w, "nvfp4", max_batch=4, max_options=8)
     try:
-        b, s, k = 2, 192, 4
-        items = synthetic_items([192, 100], ["choice", "noul"], seed=13, vocab=cfg.vocab)
+        b, s, lengths = rows
+        k = 4
+        items = synthetic_items(lengths, ["choice", "noul", "score", "choice"][:b], seed=13, vocab=cfg.vocab)
         nf.run(nf.capture(b, s, k, False), pack(items, b, s, k, cfg.pad_token_id))
         T, K = b * s, intermediate
         col_blocks = 4 * ((K + 255) // 256)
@@ -291,8 +300,9 @@ def test_token_tables_match_the_computed_start(precision, b):
 
 
 @pytest.mark.parametrize("precision", ["fp8", "nvfp4"])
-@pytest.mark.parametrize("hidden", [256, 768])
-def test_layernorm_quantised_outputs_match_oracle(precision, hidden):
+@pytest.mark.parametrize("hidden, rows", [(256, (2, 192, [192, 100])), (768, (2, 192, [192, 100])),
+                                          (256, (4, 512, [512, 200, 512, 64])), (768, (4, 512, [512, 511, 40, 512]))])
+def test_layernorm_quantised_outputs_match_oracle(precision, hidden, rows):
     """LayerNorm rows with a quantised output (add_norm, model.py:15-19, then
     _quantize_rows / the NVFP4 quantiser) against the oracle.  Replaying only
     the row kernels leaves the MLP norm of the embedding-norm output as the
@@ -305,8 +315,9 @@ def test_layernorm_quantised_outputs_match_oracle(precision, hidden):
     w = seeded_weights(cfg, seed=17)
     nf = NativeForward(0, cfg, w, precision, max_batch=4, max_options=8)
     try:
-        b, s, k = 2, 192, 4
-        items = synthetic_items([192, 100], ["choice", "noul"], seed=29, vocab=cfg.vocab)
+        b, s, lengths = rows
+        k = 4
+        items = synthetic_items(lengths, ["choice", "noul", "score", "choice"][:b], seed=29, vocab=cfg.vocab)
         inp = pack(items, b, s, k, cfg.pad_token_id)
         slot = nf.capture(b, s, k, False)
         nf.run(slot, inp)
