@@ -133,12 +133,7 @@ DEVI uint32_t visible_mask(uint32_t bits, int base, int lo, int hi) {
   return bits & from & to;
 }
 
-// 2^x on the SFU (flushes results below 2^-126 to zero; 2^-inf = 0).
-DEVI float ex2(float x) {
-  float y;
-  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
-  return y;
-}
+DEVI float ex2(float x) { return ex2_approx(x); }
 
 // Max over the visible scores of 32 consecutive keys.
 DEVI float masked_max(const uint32_t (&r)[32], uint32_t vis, float m) {
@@ -177,8 +172,6 @@ DEVI void probs(const uint32_t (&r)[32], uint32_t vis, float ms, float& l, uint3
   }
 }
 
-// Byte offset of 16-byte chunk j of row r in a 128-byte-swizzled tile.
-DEVI uint32_t sw128_offset(int r, int j) { return (r >> 3) * 1024 + (r & 7) * 128 + ((j ^ (r & 7)) << 4); }
 
 }  // namespace
 

@@ -258,6 +258,18 @@ DEVI float4 ld_dsmem_f32x4(uint32_t addr) {
                : "r"(addr));
   return v;
 }
+// 2^x on the SFU (flushes results below 2^-126 to zero; 2^-inf = 0).
+DEVI float ex2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// Byte offset of 16-byte chunk j of row r in a 128-byte-swizzled tile (rows
+// of 128 bytes, 8-row groups 1024 bytes apart), the layout TMA writes and the
+// MMA's sw128 descriptors read.
+DEVI uint32_t sw128_offset(int r, int j) { return (r >> 3) * 1024 + (r & 7) * 128 + ((j ^ (r & 7)) << 4); }
+
 // Asynchronous store into another CTA's shared memory (cluster address) that
 // counts its bytes on that CTA's mbarrier (cluster address).
 DEVI void st_async_f32(uint32_t addr, float v, uint32_t bar) {
