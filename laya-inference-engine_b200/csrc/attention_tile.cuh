@@ -1,8 +1,11 @@
-// Attention tile arithmetic shared by the attention kernels and the fused
-// batch-1 attention + output projection: 64 queries x 64 keys of one head,
-// four warps of 16 queries, mma.sync m16n8k16 (bf16 in, fp32 accumulate),
-// online softmax in fp32 with P rounded to bf16 for P.V (as FlashAttention
-// does), rotary embedding of staged rows (rope_qkv, kernels.py:62-93).
+// Attention tile arithmetic of the fused batch-1 attention + output
+// projection (gemm_attn.cu): 64 queries x 64 keys of one head, four warps of
+// 16 queries, register-level tensor-core tiles (mma.sync m16n8k16, bf16 in,
+// fp32 accumulate), online softmax in fp32 with P rounded to bf16 for P.V (as
+// FlashAttention does); and the rotary embedding of staged rows (rope_qkv,
+// kernels.py:62-93) used by the token-table gather.  Every batched shape runs
+// attention on tcgen05 instead (attention.cu); at 64 tokens these tiles are
+// shorter than a tensor-memory round trip.
 #pragma once
 #include "common.cuh"
 

@@ -9,8 +9,9 @@
 // flight (before the programmatic-dependent-launch wait), it copies q, k and v
 // of two heads at a time from the QKV buffer (already rotated by the QKV
 // projection's epilogue) with cp.async; warps 0-3 and 4-7 each compute one
-// head's attention for the 64 query positions with the standalone attention
-// kernel's tile arithmetic and write the bf16 output straight into the MMA's
+// head's attention for the 64 query positions with register-level
+// tensor-core tiles (attention_tile.cuh: at 64 tokens shorter than a
+// tensor-memory round trip) and write the bf16 output straight into the MMA's
 // B operand stage, in the 128-byte-swizzled K-major layout a TMA load would
 // have produced.  The MMA, the split-K reduction and the residual epilogue are
 // the projection GEMM's; the epilogue also writes the LayerNorm statistics of
