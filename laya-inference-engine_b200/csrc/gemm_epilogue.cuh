@@ -15,8 +15,9 @@ namespace laya {
 // partials so that an item costs one memory round trip.
 struct EpiPre {
   float sa;
-  float4 ra, rb;          // residual rows n_lo.., n_lo+64..
-  float4 c0, c1, s0, s1;  // cos / sin at d0 and d0+32
+  float4 ra, rb;  // residual rows n_lo.., n_lo+64..
+  float4 c0, s0;  // cos / sin at d0 (the tables repeat their first 32
+                  // columns, so these serve d0+32 as well)
 };
 
 template <int KIND>
@@ -30,9 +31,7 @@ DEVI EpiPre epi_prefetch(const GemmParams& p, int m, int n_lo, bool residual, bo
   if (rope) {
     const int pos = m % p.rope_seq, d0 = n_lo & 63;
     e.c0 = *reinterpret_cast<const float4*>(p.rope_cos + (size_t)pos * 64 + d0);
-    e.c1 = *reinterpret_cast<const float4*>(p.rope_cos + (size_t)pos * 64 + d0 + 32);
     e.s0 = *reinterpret_cast<const float4*>(p.rope_sin + (size_t)pos * 64 + d0);
-    e.s1 = *reinterpret_cast<const float4*>(p.rope_sin + (size_t)pos * 64 + d0 + 32);
   }
   return e;
 }
@@ -150,9 +149,12 @@ DEVI void epilogue_rope(const GemmParams& p, int m, int n_lo, float4 lo, float4 
       h[e] += __bfloat162float(bha[e]);
     }
   }
-  const float4 c0 = pre.c0, c1 = pre.c1, s0 = pre.s0, s1 = pre.s1;
-  const float cl[4] = {c0.x, c0.y, c0.z, c0.w}, ch[4] = {c1.x, c1.y, c1.z, c1.w};
-  const float sl[4] = {s0.x, s0.y, s0.z, s0.w}, sh[4] = {s1.x, s1.y, s1.z, s1.w};
+  // cos / sin at d0 + 32 equal those at d0 (the rotary embedding's
+  // cat(freqs, freqs), built so by rope_tables)
+  const float4 c0 = pre.c0, s0 = pre.s0;
+  const float cl[4] = {c0.x, c0.y, c0.z, c0.w}, sl[4] = {s0.x, s0.y, s0.z, s0.w};
+  const float* ch = cl;
+  const float* sh = sl;
   __nv_bfloat16 ol[4], oh[4];
 #pragma unroll
   for (int e = 0; e < 4; ++e) {
