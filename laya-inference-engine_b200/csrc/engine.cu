@@ -416,7 +416,9 @@ struct Fwd {
     memset(&omap, 0, sizeof(omap));
     if (split > 1 && (size_t)(w.N / 128) * ((M + bn - 1) / bn) * split * bn * 128 <= kPartialFloats)
       p.partials = e->gpart;
-    if (split == 1 && bn >= 128) {
+    // unsplit 128-token tiles store through a TMA tile map; unsplit 64-token
+    // residual tiles move their residual rows with one
+    if (split == 1 && (bn >= 128 || (bn == 64 && epi == kEpiResidual && !ln_stats))) {
       p.tma_epilogue = output_map(&omap, p, bn);
       if (!p.tma_epilogue) fail("output tensor map rejected for a %dx%d projection", M, w.N);
     }

@@ -64,7 +64,7 @@ __global__ void __launch_bounds__(BN >= 128 ? 256 : 128, BN == 128 ? 2 : 1)
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::MAIN_BYTES);
   uint64_t* empty = full + STAGES;
   uint64_t* done = empty + STAGES;
-  uint64_t* rbar = done + 1;  // residual tile load of the TMA epilogue
+  uint64_t* rbar = done + 1;  // residual tile load of the TMA residual epilogue
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(rbar + 1);
   uint32_t* failed = tmem_slot + 1;
 
@@ -162,10 +162,20 @@ __global__ void __launch_bounds__(BN >= 128 ? 256 : 128, BN == 128 ? 2 : 1)
   }
   tc_fence_after();
   const bool wide = split == 1 && p.tma_epilogue && BN >= 128;
+  // unsplit 64-token residual tiles: residual rows in and out by TMA
+  const bool tres = BN == 64 && !LNST && split == 1 && p.tma_epilogue && p.epilogue == kEpiResidual;
   if constexpr (BN >= 128) {
     if (wide) tile_epilogue_wide<BN, KIND, 256>(p, &omap, tmem, smem, tile_n, tile_m);
   }
-  if (!wide) tile_epilogue<BN, KIND, LNST>(p, tmem, reinterpret_cast<float*>(smem), tile_n, tile_m, split, rank);
+  if constexpr (BN == 64 && !LNST) {
+    static_assert(C::MAIN_BYTES >= BN * 1024 + BN * 4, "TMA residual epilogue: accumulator, residual and scale tiles");
+    if (tres && !tile_epilogue_resid_tma<BN, KIND>(p, &omap, tmem, smem, rbar, tile_n, tile_m, limit)) {
+      record_status(p.status, kStatusGemmDoneTimeout);
+      atomicExch(failed, 1u);
+    }
+  }
+  if (!wide && !tres)
+    tile_epilogue<BN, KIND, LNST>(p, tmem, reinterpret_cast<float*>(smem), tile_n, tile_m, split, rank);
 
   // ---- teardown: drain copies still in flight after a failure, free TMEM
   if (tid == 0 && *failed) {

@@ -575,4 +575,92 @@ DEVI void tile_epilogue_wide(const GemmParams& p, const CUtensorMap* omap, uint3
   __syncthreads();
 }
 
+
+// Residual epilogue of an unsplit 64-token tile (128 threads): the fp32
+// residual tile [64 tokens][128 columns] comes in with one TMA load, issued
+// while the warps move the accumulator out of TMEM, is updated in shared
+// memory (r += bf16(scaled accumulator + bias), the same arithmetic as
+// epilogue_quad) and goes back with one TMA store; rows past p.M are clipped
+// by the tensor map.  A thread keeps one column quad (its weight scales and
+// bias) for all its tokens.  Returns false when the residual tile did not
+// arrive within `limit` (nothing is stored then; thread 0 waits once more,
+// bounded, so that a late copy does not land after the CTA has exited).
+template <int BN, int KIND>
+DEVI bool tile_epilogue_resid_tma(const GemmParams& p, const CUtensorMap* rmap, uint32_t tmem, uint8_t* smem,
+                                  uint64_t* rbar, int tile_n, int tile_m, uint64_t limit) {
+  static_assert(BN == 64, "TMA residual epilogue: 64-token tiles");
+  const int tid = threadIdx.x, warp = tid >> 5;
+  const int m_base = tile_m * BN;
+  float* P = reinterpret_cast<float*>(smem);                // [BN][128] accumulator
+  float* R = reinterpret_cast<float*>(smem + BN * 512);     // [BN][128] residual rows
+  float* S = reinterpret_cast<float*>(smem + BN * 1024);    // [BN] activation row scales
+  if (tid == 0) {
+    mbar_expect_tx(rbar, BN * 512);
+    tma_load_2d(R, rmap, rbar, tile_n * 128, m_base, policy_evict_last());
+  }
+  if (warp < 4) {
+    const uint32_t lane_addr = tmem + ((uint32_t)(warp * 32) << 16);
+#pragma unroll 1
+    for (int c = 0; c < BN; c += 32) {
+      uint32_t v[32];
+      tmem_ld32(lane_addr + c, v);
+      tmem_wait_ld();
+#pragma unroll
+      for (int j = 0; j < 32; ++j) P[(c + j) * 128 + warp * 32 + (tid & 31)] = __uint_as_float(v[j]);
+    }
+  }
+  if (KIND != kKindBf16)
+    for (int i = tid; i < BN; i += blockDim.x) S[i] = m_base + i < p.M ? p.a_scale[m_base + i] : 0.f;
+  const int q = tid & 31, n = tile_n * 128 + 4 * q;
+  float ws[4] = {1.f, 1.f, 1.f, 1.f}, bx[4] = {0.f, 0.f, 0.f, 0.f};
+  if (KIND == kKindFp8) {
+    const float4 a = *reinterpret_cast<const float4*>(p.w_scale + n);
+    ws[0] = a.x; ws[1] = a.y; ws[2] = a.z; ws[3] = a.w;
+  }
+  if (p.bias) {
+    const uint2 bu = *reinterpret_cast<const uint2*>(p.bias + n);
+    const __nv_bfloat16* bb = reinterpret_cast<const __nv_bfloat16*>(&bu);
+#pragma unroll
+    for (int e = 0; e < 4; ++e) bx[e] = __bfloat162float(bb[e]);
+  }
+  const float tsc = KIND == kKindNvfp4 ? p.w_tensor_scale : 1.f;
+  __syncthreads();
+  const bool ok = mbar_wait(rbar, 0, limit);
+  if (ok) {
+    for (int tok = tid >> 5; tok < BN; tok += blockDim.x >> 5) {
+      const float4 a = *reinterpret_cast<const float4*>(P + tok * 128 + 4 * q);
+      float x[4] = {a.x, a.y, a.z, a.w};
+      if (KIND == kKindFp8) {
+#pragma unroll
+        for (int e = 0; e < 4; ++e) x[e] = (x[e] * S[tok]) * ws[e];
+      } else if (KIND == kKindNvfp4) {
+        const float sc = S[tok] * tsc;
+#pragma unroll
+        for (int e = 0; e < 4; ++e) x[e] *= sc;
+      }
+      if (p.bias) {
+#pragma unroll
+        for (int e = 0; e < 4; ++e) x[e] += bx[e];
+      }
+      float4* rp = reinterpret_cast<float4*>(R + tok * 128 + 4 * q);
+      float4 r = *rp;
+      r.x += bf16_round(x[0]);
+      r.y += bf16_round(x[1]);
+      r.z += bf16_round(x[2]);
+      r.w += bf16_round(x[3]);
+      *rp = r;
+    }
+    fence_proxy_async_smem();
+  }
+  __syncthreads();
+  if (ok && tid == 0) {
+    tma_store_2d(rmap, R, tile_n * 128, m_base);
+    bulk_commit();
+    bulk_wait_read0();
+  }
+  if (!ok && tid == 0) mbar_wait(rbar, 0, limit);  // a late tile still lands before the CTA exits
+  __syncthreads();
+  return ok;
+}
+
 }  // namespace laya
