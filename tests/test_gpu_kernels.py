@@ -194,6 +194,43 @@ def test_fp8_activation_quantiser_is_bit_exact(intermediate, rows):
         nf.close()
 
 
+def test_residual_tiles_with_a_partial_last_tile():
+    """Unsplit 64-token residual tiles move their fp32 residual rows with one
+    TMA load and one TMA store.  11 x 450 = 4,950 token rows at d = 256 give
+    Wo and Wo2 156 such tiles, the last one 22 rows high: every row before the
+    end must be updated (padded positions included) and none past it.  The
+    final hidden rows are compared with the oracle fed with the GPU's own
+    attention and GEGLU outputs, as in test_stages_match_oracle."""
+    from laya_b200.engine import NativeForward
+    cfg = MICRO
+    w = seeded_weights(cfg, seed=5)
+    b, s, k = 11, 450, 4
+    kinds = ["choice", "score", "noul"]
+    items = synthetic_items([450] * 9 + [300, 17], [kinds[i % 3] for i in range(b)], seed=13, vocab=cfg.vocab)
+    inp = pack(items, b, s, k, cfg.pad_token_id)
+    T, d, I = b * s, cfg.hidden, cfg.intermediate
+    nf = NativeForward(0, cfg, w, "bf16", max_batch=b, max_options=8)
+    try:
+        slot = nf.capture(b, s, k, False)
+        nf.run(slot, inp)
+        attn = bf16_of(nf.read_buffer("attn", (T, d), np.uint16))
+        g = bf16_of(nf.read_buffer("g", (T, I), np.uint16))
+        h = torch.from_numpy(nf.read_buffer("h", (T, d), np.float32))
+    finally:
+        nf.close()
+    wf = {kk: torch.from_numpy(v) for kk, v in as_float32(w).items()}
+    ids = torch.from_numpy(inp["input_ids"]).reshape(-1)
+    h0 = O.layer_norm(wf["embed.tok"][ids], wf["embed.norm.w"], None, cfg.norm_eps)
+    h1 = h0 + O.linear(attn, wf["enc.0.wo"])
+    h2 = h1 + O.linear(g, wf["enc.0.wo2"])
+    qt = torch.from_numpy(inp["qtype"])
+    hf = O.layer_norm(h2, wf["final_norm.w"], None, cfg.norm_eps).view(b, s, d) + wf["type_emb"][qt][:, None, :]
+    err = (h.view(b, s, d) - hf).abs().amax(dim=-1)   # per token row
+    print("final hidden rows: max-abs", float(err.max()), "in the last tile", float(err.view(-1)[-22:].max()))
+    assert torch.isfinite(h).all()
+    assert float(err.max()) < 2e-2, float(err.max())
+
+
 @pytest.mark.parametrize("s,length", [(64, 64), (64, 37), (40, 40)])
 def test_fused_attention_projection_matches_oracle(s, length):
     """One short sequence in bf16 runs attention inside the Wo projection and
