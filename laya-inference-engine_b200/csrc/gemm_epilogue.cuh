@@ -624,8 +624,9 @@ DEVI bool tile_epilogue_resid_tma(const GemmParams& p, const CUtensorMap* rmap, 
     for (int e = 0; e < 4; ++e) bx[e] = __bfloat162float(bb[e]);
   }
   const float tsc = KIND == kKindNvfp4 ? p.w_tensor_scale : 1.f;
-  __syncthreads();
-  const bool ok = mbar_wait(rbar, 0, limit);
+  // one CTA-wide verdict on the residual tile (the barrier also publishes P
+  // and S), so that every thread takes the same path
+  const bool ok = __syncthreads_and(mbar_wait(rbar, 0, limit)) != 0;
   if (ok) {
     for (int tok = tid >> 5; tok < BN; tok += blockDim.x >> 5) {
       const float4 a = *reinterpret_cast<const float4*>(P + tok * 128 + 4 * q);
